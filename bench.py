@@ -1,0 +1,407 @@
+"""Throughput of OmniVoice's generator hot path on B200.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload c2|c1|c3|c5|c4] [--noise device|reference]
+
+A "step" is one full 32-step CFG unmasking generation of the workload.
+The default workload is BASELINE config 2 (120 text tokens + 250 masked
+frames = one 10 s utterance) on every GPU: independent utterances are
+replicated across ranks with no collective on the data path (weak
+scaling).  `--workload c4` runs the batched config (64 utterances,
+partitioned across ranks by longest-processing-time, strong scaling).
+
+value: audio seconds generated per second, whole job, inputs resident in
+HBM, device time (CUDA events on the generator's stream, max over ranks).
+e2e:   the same metric through the C-ABI with host buffers (upload of the
+inputs and download of the codes inside the timed region), wall clock.
+Rank 0 prints one JSON line.  `--impl reference` times the CPU restatement
+of the reference generator (oracle/, the reference's own generator is HIP
+code that cannot run here) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "audio-sec generated per sec (32-step CFG) at 1/2/4/8 B200; per-step backbone ms"
+FRAME_RATE = 25.0
+VOCAB = 151936
+
+
+# ------------------------------------------------------------- workloads
+
+def _input(rng, text, ref_frames, target):
+    from omnivoice_b200 import ConditionalInput
+    text_ids = rng.integers(0, VOCAB, size=text).tolist()
+    ref = rng.integers(0, 1024, size=(8, ref_frames)).astype(np.int32) if ref_frames else None
+    return ConditionalInput.build(text_ids, ref, target)
+
+
+WORKLOADS = {
+    "c1": ("config1: 40 text + 100 masked frames (4 s), 32-step CFG", 0, [(40, 0, 100)]),
+    "c2": ("config2: 120 text + 250 masked frames (10 s), 32-step CFG", 1, [(120, 0, 250)]),
+    "c3": ("config3: 180 text + 150 reference + 375 masked frames (15 s), 32-step CFG", 2,
+           [(180, 150, 375)]),
+    "c5": ("config5: 300 text + 375 reference + 750 masked frames (30 s), 32-step CFG", 3,
+           [(300, 375, 750)]),
+}
+
+
+def batched_set(seed=4, count=64):
+    """64 utterances, F ~ U[50, 750], text = round(0.4 F),
+    half with 125-250 frames of reference codes."""
+    rng = np.random.default_rng(seed)
+    frames = rng.integers(50, 751, size=count)
+    with_ref = set(rng.permutation(count)[: count // 2].tolist())
+    specs = []
+    for i, f in enumerate(frames):
+        ref = int(rng.integers(125, 251)) if i in with_ref else 0
+        specs.append((int(round(0.4 * f)), ref, int(f)))
+    return rng, specs
+
+
+def utterance_cost(text, ref, target):
+    L = text + ref + target
+    R = L + target
+    return 32 * (R * 880.80e6 + 229376.0 * (L * L + target * target) + 2 * target * 16.79e6)
+
+
+def lpt_partition(specs, ranks):
+    """Longest-processing-time-first assignment of utterances to ranks."""
+    order = sorted(range(len(specs)), key=lambda i: -utterance_cost(*specs[i]))
+    load = [0.0] * ranks
+    parts = [[] for _ in range(ranks)]
+    for i in order:
+        r = min(range(ranks), key=lambda k: load[k])
+        parts[r].append(i)
+        load[r] += utterance_cost(*specs[i])
+    return parts, load
+
+
+def make_workload(name, rank, world):
+    if name == "c4":
+        rng, specs = batched_set()
+        inputs_all = [_input(rng, *s) for s in specs]
+        parts, load = lpt_partition(specs, world)
+        mine = parts[rank]
+        desc = "config4: 64 utterances, F~U[50,750], LPT-partitioned across ranks"
+        total_audio = sum(s[2] for s in specs) / FRAME_RATE
+        return (desc, [inputs_all[i] for i in mine], [1000 + i for i in mine], total_audio,
+                "strong", {"imbalance_max_over_mean": max(load) / (sum(load) / world)})
+    desc, seed, specs = WORKLOADS[name]
+    rng = np.random.default_rng(seed)
+    inputs = [_input(rng, *s) for s in specs]
+    total_audio = world * sum(s[2] for s in specs) / FRAME_RATE
+    return desc, inputs, [seed + 100 * rank for _ in specs], total_audio, "weak", {}
+
+
+# -------------------------------------------------------------- helpers
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during timing."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: str):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.gpu, f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) != 6:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for name, value in zip(names, parts[2:]):
+                if value.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def measured_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        d = json.loads(path.read_text())
+        return d.get("bf16_tflops"), d.get("hbm_gbs"), "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+def cpu_baseline(inputs, threads):
+    """The oracle (CPU restatement of the reference generator) on one step
+    of the workload's first utterance, extrapolated to 32 steps."""
+    from oracle import binding
+    binding.oracle().oc_set_threads(threads)
+    cfg = binding.config()
+    model = binding.OracleModel(cfg, 0)
+    inp = inputs[0]
+    t0 = time.perf_counter()
+    logits = model.forward(inp.ids, inp.audio_start, inp.target_frames)
+    pred, conf = binding.score(logits, inp.target_frames)
+    codes = np.full((8, inp.target_frames), 1024, np.int32)
+    binding.select(8 * inp.target_frames // 32, pred, conf, codes,
+                   gumbel=binding.reference_gumbel(0, 8 * inp.target_frames))
+    step_s = time.perf_counter() - t0
+    model.close()
+    audio = inp.target_frames / FRAME_RATE
+    return {"value": audio / (32 * step_s), "unit": "audio_s/s", "cores": threads, "kind": "port",
+            "sample": f"one forward+score+select step of the workload's first utterance "
+                      f"({step_s:.2f} s), x32 extrapolated to the full generation"}
+
+
+# ------------------------------------------------------------------ arms
+
+def run_reference(args, rank, world):
+    """--impl reference: the CPU restatement timed on the host cores.
+
+    Each step is a bounded sample of one generation of the workload's first
+    utterance: a forward with 0 layers (embedding + head) and one with 2
+    layers are timed, with the scoring and the position choice; the full
+    generation time is extrapolated as 32 x (t0 + 28 (t2 - t0) / 2 + t_tail)."""
+    if rank != 0:
+        return
+    from oracle import binding
+    threads = os.cpu_count() or 1
+    binding.oracle().oc_set_threads(threads)
+    desc, inputs, seeds, total_audio, scaling, extra = make_workload(args.workload, 0, 1)
+    model = binding.OracleModel(binding.config(), 0)
+    inp = inputs[0]
+    F = inp.target_frames
+
+    def one_step():
+        s = time.perf_counter()
+        model.forward(inp.ids, inp.audio_start, F, layers=0)
+        t0 = time.perf_counter() - s
+        s = time.perf_counter()
+        logits = model.forward(inp.ids, inp.audio_start, F, layers=2)
+        t2 = time.perf_counter() - s
+        s = time.perf_counter()
+        pred, conf = binding.score(logits, F)
+        binding.select(8 * F // 32, pred, conf, np.full((8, F), 1024, np.int32),
+                       gumbel=binding.reference_gumbel(0, 8 * F))
+        t_tail = time.perf_counter() - s
+        return 32 * (t0 + 28 * max(t2 - t0, 0.0) / 2 + t_tail)
+
+    for _ in range(max(1, args.warmup)):
+        one_step()
+    gen_s = float(np.mean([one_step() for _ in range(args.steps)]))
+    value = (F / FRAME_RATE) / gen_s
+    line = {"metric": METRIC, "value": value, "unit": "audio_s/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": gen_s * 1e3,
+            "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": desc + " (first utterance)",
+                       "implementation": "oracle/: CPU restatement of the reference generator; "
+                                         "the reference's generator is HIP-only"},
+            "cpu_baseline": {"value": value, "unit": "audio_s/s", "cores": threads, "kind": "port",
+                             "sample": "per step: forwards with 0 and 2 layers + score + select "
+                                       "timed, extrapolated to 28 layers and 32 steps"},
+            "e2e": {"value": value, "unit": "audio_s/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    model.close()
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank, world, local_rank, dist):
+    import torch
+
+    from omnivoice_b200 import DecodingConfig, Generator
+    from omnivoice_b200 import _native as N
+
+    torch.cuda.set_device(local_rank)
+    lib = N.lib()
+    desc, inputs, seeds, total_audio, scaling, extra = make_workload(args.workload, rank, world)
+    dec = DecodingConfig()
+    gen = Generator.synthetic(weight_seed=0, device=local_rank)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local_rank}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # Device-resident timing: inputs uploaded once, K full generations.
+    gen.prepare(inputs, dec, seeds, noise=args.noise)
+    st = gen.stats()
+    stream = st.stream
+    for _ in range(args.warmup):
+        gen.run()
+    ev0, ev1 = ctypes.c_void_p(), ctypes.c_void_p()
+    N.check(lib.ov_event_create(ctypes.byref(ev0)))
+    N.check(lib.ov_event_create(ctypes.byref(ev1)))
+    N.check(lib.ov_stream_sync(stream))
+    gpu_index = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
+    gpu_index = gpu_index[local_rank] if len(gpu_index) > local_rank and gpu_index[0] else str(local_rank)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(gpu_index) as clocks:
+        N.check(lib.ov_event_record(ev0, stream))
+        for _ in range(args.steps):
+            gen.run()
+        N.check(lib.ov_event_record(ev1, stream))
+        N.check(lib.ov_event_sync(ev1))
+    ms = ctypes.c_float()
+    N.check(lib.ov_event_elapsed_ms(ev0, ev1, ctypes.byref(ms)))
+    torch.cuda.synchronize()
+    barrier()
+    t_max = max_over_ranks(ms.value)
+    ms_per_gen = t_max / args.steps
+    value = total_audio * args.steps / (t_max / 1e3)
+    results = gen.fetch()
+    assert all(((r.codes >= 0) & (r.codes < 1024)).all() for r in results)
+
+    # Per-kernel-class device time of one step (CUDA events between the
+    # kernels of a captured step, on the generator's stream).
+    prof = gen.profile_step()
+    st = gen.stats()
+    backbone_ms = sum(k["ms"] for k in prof if k["name"] not in ("score", "select"))
+    gemms = [k for k in prof if k["name"].startswith("gemm")]
+    gemm_ms = sum(k["ms"] for k in gemms)
+    gemm_flops = sum(k["flops"] for k in gemms)
+    gemm_launches = sum(k["launches"] for k in gemms)
+    tflops_peak, hbm_peak, peak_kind = measured_peaks()
+    achieved = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else 0.0
+
+    # End to end through the C-ABI with host buffers.
+    for _ in range(max(1, args.warmup // 2)):
+        gen.generate_batch(inputs, dec, seeds, noise=args.noise)
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        gen.generate_batch(inputs, dec, seeds, noise=args.noise)
+    torch.cuda.synchronize()
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    st_e2e = gen.stats()
+    e2e_value = total_audio * args.steps / e2e_s
+
+    base = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        base = cpu_baseline(inputs, os.cpu_count() or 1)
+    gen.close()
+
+    if rank != 0:
+        return
+    launches_per_gen = st.kernels_per_step * st.steps_run + st.kernels_per_reset
+    line = {
+        "metric": METRIC, "value": value, "unit": "audio_s/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_gen,
+        "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic",
+        "config": {"workload": desc, "rows_per_step": st.rows,
+                   "steps_per_generation": st.steps_run,
+                   "gflop_per_step": st.flops_per_step / 1e9, "noise": args.noise,
+                   "weights": "random init N(0,0.02) (synthetic), fp16",
+                   "l2_policy": "inputs larger than L2: every step streams 0.93 GB of weights",
+                   "parallelism": f"dp{world} ({'replicas' if scaling == 'weak' else 'LPT partition'}), no collectives",
+                   **extra},
+        "backbone_ms_per_step": backbone_ms,
+        "full_step_ms": ms_per_gen / max(st.steps_run, 1),
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": tflops_peak,
+                     "unit": "TFLOP/s", "frac": achieved / tflops_peak if tflops_peak else None,
+                     "traffic": None, "kernel": "tcgen05 GEMM (all backbone + head launches)",
+                     "launches_per_step": gemm_launches, "peak_kind": peak_kind},
+        "cpu_baseline": base,
+        "clocks": clocks.summary(),
+        "e2e": {"value": e2e_value, "unit": "audio_s/s",
+                "h2d_bytes_per_step": st_e2e.h2d_bytes, "d2h_bytes_per_step": st_e2e.d2h_bytes,
+                "timing": "wall clock around ov_generator_generate_batch"},
+        "gpu_launches": launches_per_gen * args.steps,
+        "kernels": [{k["name"]: round(k["ms"], 4), "launches": k["launches"],
+                     "tflops": round(k["flops"] / (k["ms"] / 1e3) / 1e12, 1) if k["flops"] and k["ms"] else None,
+                     "gbs": round(k["bytes"] / (k["ms"] / 1e3) / 1e9, 1) if k["bytes"] and k["ms"] else None}
+                    for k in prof],
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    parser = argparse.ArgumentParser(description=__doc__,
+                                     formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=20)
+    parser.add_argument("--warmup", type=int, default=3)
+    parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    parser.add_argument("--workload", choices=["c1", "c2", "c3", "c4", "c5"], default="c2")
+    parser.add_argument("--noise", choices=["device", "reference"], default="device")
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    args = parser.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as tdist
+        torch.cuda.set_device(local_rank)
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                 device_id=torch.device(f"cuda:{local_rank}"))
+        dist = tdist
+    try:
+        if args.impl == "reference":
+            run_reference(args, rank, world)
+        else:
+            run_ours(args, rank, world, local_rank, dist)
+    finally:
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
