@@ -110,7 +110,9 @@ typedef struct {
  * x, w are K-major with row strides ldx / in elements (multiples of 8);
  * y's row stride ldy is in elements of the output type.  `workspace`
  * (optional, may be NULL) enables a deterministic split-K for short-M
- * residual GEMMs; ov_gemm_workspace_bytes gives its size. */
+ * residual GEMMs; ov_gemm_workspace_bytes gives its size.  Its first 1024
+ * bytes hold arrival counters: zero them once before the first call (every
+ * call leaves them zero again); calls sharing a workspace must not overlap. */
 int ov_gemm_f16(const uint16_t* x, size_t ldx, const uint16_t* w, void* y, size_t ldy,
                 size_t rows, size_t in, size_t out, int epilogue,
                 const ov_epilogue_args* args, void* workspace, size_t workspace_bytes,
@@ -119,6 +121,7 @@ size_t ov_gemm_workspace_bytes(size_t rows, size_t in, size_t out, int epilogue)
 /* Host helper: interleave [gate(width) | up(width)] rows of a float16 weight
  * [2*width][in] into groups of OV_SWIGLU_GROUP rows (layout described above). */
 int ov_interleave_gate_up(const uint16_t* gate_up, size_t width, size_t in, uint16_t* output);
+
 
 /* ------------------------------------------------------------ attention */
 

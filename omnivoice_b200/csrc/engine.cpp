@@ -546,7 +546,8 @@ struct EventMarker : Engine::Marker {
     cudaEvent_t e = nullptr;
     Check(cudaEventCreate(&e), "cudaEventCreate");
     events.push_back(e);
-    Check(cudaEventRecord(e, stream), "cudaEventRecord");
+    // External: a timed event-record node in the captured graph.
+    Check(cudaEventRecordWithFlags(e, stream, cudaEventRecordExternal), "cudaEventRecord");
     kinds.push_back(kind);
     flops.push_back(f);
     bytes.push_back(b);

@@ -36,6 +36,9 @@ constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kThreads = 192;
 constexpr int kRingBytes = 196608;
+// Split-K workspace: arrival counters first (zero between launches), then
+// the partial tiles.
+constexpr size_t kCounterBytes = 1024;
 
 template <int BN>
 struct TileConfig {
@@ -367,7 +370,7 @@ size_t GemmWorkspaceBytes(int M, int N, int K, int epilogue, int sms) {
   const GemmShapeChoice c = ChooseGemmShape(M, N, K, epilogue, true, sms);
   if (c.splits <= 1) return 0;
   const size_t tiles = static_cast<size_t>(Tiles(M, N, c.bn));
-  return tiles * c.splits * kBM * c.bn * sizeof(float) + tiles * sizeof(uint32_t) + 256;
+  return kCounterBytes + tiles * c.splits * kBM * c.bn * sizeof(float);
 }
 
 void PlanGemm(GemmPlan* plan, const uint16_t* x, int64_t ldx, const uint16_t* w, int64_t w_rows,
@@ -413,10 +416,12 @@ void PlanGemm(GemmPlan* plan, const uint16_t* x, int64_t ldx, const uint16_t* w,
   a.y = y;
   a.err = DeviceErrorWord();
   if (choice.splits > 1) {
-    const size_t tiles = static_cast<size_t>(Tiles(M, N, choice.bn));
-    a.partials = static_cast<float*>(workspace);
-    a.counters = reinterpret_cast<uint32_t*>(static_cast<char*>(workspace) +
-                                             tiles * choice.splits * kBM * choice.bn * sizeof(float));
+    // Counters live at a fixed place, ahead of the partial tiles, so a
+    // workspace shared by products of different shapes keeps them zero
+    // (every split-K launch leaves its counters at zero).
+    OV_REQUIRE(Tiles(M, N, choice.bn) * sizeof(uint32_t) <= kCounterBytes, "split-K tile count");
+    a.counters = static_cast<uint32_t*>(workspace);
+    a.partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterBytes);
   }
   if (ea != nullptr) {
     a.q_norm = ea->q_norm;

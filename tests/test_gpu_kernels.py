@@ -95,8 +95,9 @@ def test_rmsnorm_and_gather(rows, width):
     out = torch.empty(rows, width, device="cuda", dtype=torch.float16)
     ok(N.lib().ov_rmsnorm(p(xd), p(wd), p(out), rows, width, 1e-6, stream()))
     idx = torch.randint(0, rows, (7,), generator=g, dtype=torch.int32)
+    idxd = idx.cuda()
     out2 = torch.empty(7, width, device="cuda", dtype=torch.float16)
-    ok(N.lib().ov_gather_rmsnorm(p(xd), p(idx.cuda()), 7, p(wd), p(out2), width, 1e-6, stream()))
+    ok(N.lib().ov_gather_rmsnorm(p(xd), p(idxd), 7, p(wd), p(out2), width, 1e-6, stream()))
     torch.cuda.synchronize()
     xd64 = x.double()
     ref = (w.double() * (xd64 * torch.rsqrt(xd64.pow(2).mean(-1, keepdim=True) + 1e-6))).numpy()
@@ -137,13 +138,16 @@ def test_qknorm_rope_standalone():
     pos = torch.randint(0, 2000, (rows,), generator=g, dtype=torch.int32)
     cos, sin = rope_tables(4096)
     out = torch.empty(rows, width, device="cuda", dtype=torch.float16)
-    ok(N.lib().ov_qknorm_rope(p(qkv.cuda()), width, p(qn.cuda()), p(kn.cuda()), p(pos.cuda()),
-                              p(cos.cuda()), p(sin.cuda()), 4096, rows, heads, kv, 128, 1e-6,
-                              p(out), width, stream()))
+    # Device copies stay referenced until the kernel has run.
+    d = [t.cuda() for t in (qkv, qn, kn, pos, cos, sin)]
+    ok(N.lib().ov_qknorm_rope(p(d[0]), width, p(d[1]), p(d[2]), p(d[3]), p(d[4]), p(d[5]), 4096,
+                              rows, heads, kv, 128, 1e-6, p(out), width, stream()))
     torch.cuda.synchronize()
     ref = qknorm_rope_reference(qkv, qn, kn, pos, cos, sin, heads, kv)
     got = out.cpu().double().numpy()
-    assert (np.abs(got - ref) <= 2 * half_ulp(ref)).all()
+    # Two half ulps, plus float32 rounding of the rotation's O(1) terms for
+    # outputs that cancel towards zero.
+    assert (np.abs(got - ref) <= 2 * half_ulp(ref) + 1e-5).all()
 
 
 def test_swiglu_standalone():
@@ -151,7 +155,8 @@ def test_swiglu_standalone():
     rows, width = 50, 3072
     gu = torch.randn(rows, 2 * width, generator=g) * 3
     out = torch.empty(rows, width, device="cuda", dtype=torch.float16)
-    ok(N.lib().ov_swiglu(p(gu.cuda()), rows, width, p(out), stream()))
+    gud = gu.cuda()
+    ok(N.lib().ov_swiglu(p(gud), rows, width, p(out), stream()))
     torch.cuda.synchronize()
     gd = gu.double()
     ref = (gd[:, :width] / (1 + torch.exp(-gd[:, :width])) * gd[:, width:]).numpy()
@@ -280,7 +285,8 @@ def test_attention_varlen(lengths):
         bounds.append(bounds[-1] + n)
     cu = torch.tensor(bounds, dtype=torch.int32).cuda()
     out = torch.full((rows, heads * 128), float("nan"), device="cuda", dtype=torch.float16)
-    ok(N.lib().ov_attention_varlen(p(qkv.cuda()), width, rows, p(cu), len(lengths),
+    qkv_d = qkv.cuda()
+    ok(N.lib().ov_attention_varlen(p(qkv_d), width, rows, p(cu), len(lengths),
                                    max(lengths), heads, kv, 128, 1.0 / np.sqrt(128), p(out),
                                    heads * 128, stream()))
     torch.cuda.synchronize()
@@ -333,8 +339,9 @@ def test_select_matches_oracle_bit_exact(oracle_lib, frames, temperature):
     dcodes = torch.from_numpy(codes.reshape(C, frames)).cuda()
     dwhen = torch.full((C, frames), -1, dtype=torch.int32, device="cuda")
     g_dev = torch.from_numpy(gumbel).cuda() if gumbel is not None else None
+    pd, cd = torch.from_numpy(pred).cuda(), torch.from_numpy(conf).cuda()
     ok(N.lib().ov_select_positions(
-        p(torch.from_numpy(pred).cuda()), p(torch.from_numpy(conf).cuda()), C, frames, count, 5.0,
+        p(pd), p(cd), C, frames, count, 5.0,
         temperature, N.OV_NOISE_BUFFER if temperature > 0 else N.OV_NOISE_NONE,
         p(g_dev) if g_dev is not None else None, 0, 9, 1024, p(dcodes), p(dwhen), p(ids), R,
         L - frames, L, stream()))
@@ -362,8 +369,8 @@ def test_select_device_noise_picks_only_masked_slots():
     pred = rng.integers(0, 1024, size=n).astype(np.int32)
     conf = rng.normal(-3, 1, size=n).astype(np.float32)
     dcodes = torch.from_numpy(codes).cuda()
-    ok(N.lib().ov_select_positions(p(torch.from_numpy(pred).cuda()),
-                                   p(torch.from_numpy(conf).cuda()), C, frames, 300, 5.0, 5.0,
+    pd, cd = torch.from_numpy(pred).cuda(), torch.from_numpy(conf).cuda()
+    ok(N.lib().ov_select_positions(p(pd), p(cd), C, frames, 300, 5.0, 5.0,
                                    N.OV_NOISE_DEVICE, None, 1234, 3, 1024, p(dcodes), None, None,
                                    0, 0, 0, stream()))
     torch.cuda.synchronize()
