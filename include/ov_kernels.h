@@ -122,6 +122,27 @@ size_t ov_gemm_workspace_bytes(size_t rows, size_t in, size_t out, int epilogue)
  * [2*width][in] into groups of OV_SWIGLU_GROUP rows (layout described above). */
 int ov_interleave_gate_up(const uint16_t* gate_up, size_t width, size_t in, uint16_t* output);
 
+/* ov_gemm_f16 for callers that cannot allocate device memory.  No
+ * counterpart in the reference: it is an addition of this library.
+ *
+ * Some callers cannot call cudaMalloc: a host process that has handed all
+ * of the GPU's memory to its own pool, or code on a latency-critical path
+ * where cudaMalloc / cudaFree would block on or synchronise the device.
+ * This entry point allocates nothing.  Its split-K scratch is a 10 MiB
+ * file-scope device array that every GPU loading the library holds until
+ * the process exits; bounded waits report into a status word kept with it.
+ * Inputs and outputs are the caller's, as for ov_gemm_f16.
+ *   - The first call on a device sets up that device (looks up the array's
+ *     device address with that device current and clears its counters);
+ *     make that first call before any stream capture.
+ *   - Products that would need more than 10 MiB of split-K scratch are
+ *     rejected with OV_ERR_INVALID (none do on a 148-SM B200).
+ *   - Every call shares the array, which keeps the last call's contents:
+ *     calls that overlap on the GPU (different streams, or different host
+ *     threads on one device) race and must be serialised by the caller. */
+int ov_gemm_f16_noalloc(const uint16_t* x, size_t ldx, const uint16_t* w, void* y, size_t ldy,
+                        size_t rows, size_t in, size_t out, int epilogue,
+                        const ov_epilogue_args* args, ov_stream_t stream);
 
 /* ------------------------------------------------------------ attention */
 

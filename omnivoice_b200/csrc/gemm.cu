@@ -23,6 +23,7 @@
 
 #include <algorithm>
 #include <cstdint>
+#include <mutex>
 
 #include "gemm.hpp"
 #include "internal.hpp"
@@ -375,7 +376,8 @@ size_t GemmWorkspaceBytes(int M, int N, int K, int epilogue, int sms) {
 
 void PlanGemm(GemmPlan* plan, const uint16_t* x, int64_t ldx, const uint16_t* w, int64_t w_rows,
               int b_row_offset, void* y, int64_t ldy, int M, int N, int K, int epilogue,
-              const ov_epilogue_args* ea, void* workspace, size_t workspace_bytes, int sms) {
+              const ov_epilogue_args* ea, void* workspace, size_t workspace_bytes, int sms,
+              uint32_t* err) {
   OV_REQUIRE(M > 0 && N > 0 && K > 0, "empty GEMM");
   OV_REQUIRE(K % kBK == 0, "GEMM K must be a multiple of 64");
   OV_REQUIRE(ldx % 8 == 0 && ldx >= K, "x row stride must be a multiple of 8 and >= K");
@@ -414,7 +416,7 @@ void PlanGemm(GemmPlan* plan, const uint16_t* x, int64_t ldx, const uint16_t* w,
   a.b_row_offset = b_row_offset;
   a.ldy = ldy;
   a.y = y;
-  a.err = DeviceErrorWord();
+  a.err = err != nullptr ? err : DeviceErrorWord();
   if (choice.splits > 1) {
     // Counters live at a fixed place, ahead of the partial tiles, so a
     // workspace shared by products of different shapes keeps them zero
@@ -480,6 +482,73 @@ void LaunchGemm(const GemmPlan& p, cudaStream_t stream) {
 
 }  // namespace ovb
 
+// ------------------------------------------------ allocation-free variant
+//
+// ov_gemm_f16_noalloc takes its split-K scratch from this file-scope device
+// array instead of a caller-supplied workspace.  Every GPU that loads the
+// library holds it until the process exits.  In host code the array's name
+// only stands for the symbol, so its device address is looked up with
+// cudaGetSymbolAddress once per device (with that device current) and that
+// address is what the kernel receives.
+constexpr size_t kNoAllocScratchBytes = size_t{10} << 20;  // 10 MiB per device
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+// Bounded waits of this variant report into this word (it allocates nothing,
+// so it cannot use the lazily allocated device error word).
+static __device__ __align__(256) uint32_t g_noalloc_status[64];
+
+namespace ovb {
+namespace {
+
+constexpr int kNoAllocDevices = 64;
+std::mutex g_noalloc_mutex;
+uint8_t* g_noalloc_scratch_ptr[kNoAllocDevices] = {};
+uint32_t* g_noalloc_status_ptr[kNoAllocDevices] = {};
+
+template <int BN, int EPI>
+void SetSmemDirect() {
+  Check(cudaFuncSetAttribute(gemm_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(TileConfig<BN>::kSmemBytes)),
+        "cudaFuncSetAttribute(max dynamic shared memory)");
+}
+
+// Once per device, with it current: device addresses of the static arrays,
+// cleared split-K counters, and the kernels' shared-memory limits.
+void NoAllocSetup(uint8_t** scratch, uint32_t** status) {
+  int device = 0;
+  Check(cudaGetDevice(&device), "cudaGetDevice");
+  if (device < 0 || device >= kNoAllocDevices) throw Error(OV_ERR_INVALID, "device index");
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_scratch_ptr[device] == nullptr) {
+    void* sp = nullptr;
+    void* tp = nullptr;
+    Check(cudaGetSymbolAddress(&sp, g_noalloc_scratch), "cudaGetSymbolAddress(scratch)");
+    Check(cudaGetSymbolAddress(&tp, g_noalloc_status), "cudaGetSymbolAddress(status)");
+    Check(cudaMemset(sp, 0, kCounterBytes), "clear split-K counters");
+    Check(cudaMemset(tp, 0, sizeof(uint32_t) * 64), "clear status word");
+    SetSmemDirect<128, OV_EPI_STORE_F32>();
+    SetSmemDirect<256, OV_EPI_STORE_F32>();
+    SetSmemDirect<128, OV_EPI_ACCUM_F32>();
+    SetSmemDirect<256, OV_EPI_ACCUM_F32>();
+    SetSmemDirect<128, OV_EPI_SWIGLU_F16>();
+    SetSmemDirect<256, OV_EPI_SWIGLU_F16>();
+    SetSmemDirect<128, OV_EPI_QKNORM_ROPE_F16>();
+    g_noalloc_status_ptr[device] = static_cast<uint32_t*>(tp);
+    g_noalloc_scratch_ptr[device] = static_cast<uint8_t*>(sp);
+  }
+  *scratch = g_noalloc_scratch_ptr[device];
+  *status = g_noalloc_status_ptr[device];
+}
+
+template <int BN, int EPI>
+void LaunchDirect(const GemmPlan& p, cudaStream_t stream) {
+  gemm_kernel<BN, EPI><<<p.grid, kThreads, TileConfig<BN>::kSmemBytes, stream>>>(p.map_a, p.map_b,
+                                                                                p.args);
+  Check(cudaGetLastError(), "gemm kernel launch");
+}
+
+}  // namespace
+}  // namespace ovb
+
 using namespace ovb;
 
 extern "C" {
@@ -519,6 +588,41 @@ int ov_interleave_gate_up(const uint16_t* gate_up, size_t width, size_t in, uint
       const uint16_t* up = gate_up + (width + j) * in;
       std::copy(gate, gate + in, output + (2 * g * group + r) * in);
       std::copy(up, up + in, output + (2 * g * group + group + r) * in);
+    }
+  });
+}
+
+int ov_gemm_f16_noalloc(const uint16_t* x, size_t ldx, const uint16_t* w, void* y, size_t ldy,
+                        size_t rows, size_t in, size_t out, int epilogue,
+                        const ov_epilogue_args* args, ov_stream_t stream) {
+  return Guard("ov_gemm_f16_noalloc: ", [&] {
+    uint8_t* scratch = nullptr;
+    uint32_t* status = nullptr;
+    NoAllocSetup(&scratch, &status);
+    if (rows == 0) return;
+    const int sms = SmCount();
+    const size_t need = GemmWorkspaceBytes(static_cast<int>(rows), static_cast<int>(out),
+                                           static_cast<int>(in), epilogue, sms);
+    if (need > kNoAllocScratchBytes)
+      throw Error(OV_ERR_INVALID, "needs " + std::to_string(need) +
+                                      " bytes of split-K scratch, more than the " +
+                                      std::to_string(kNoAllocScratchBytes) + "-byte static array");
+    GemmPlan plan;
+    PlanGemm(&plan, x, static_cast<int64_t>(ldx), w, static_cast<int64_t>(out), 0, y,
+             static_cast<int64_t>(ldy), static_cast<int>(rows), static_cast<int>(out),
+             static_cast<int>(in), epilogue, args, scratch, kNoAllocScratchBytes, sms, status);
+    const cudaStream_t s = AsStream(stream);
+    switch (plan.epilogue * 1000 + plan.bn) {
+      case OV_EPI_STORE_F32 * 1000 + 128: LaunchDirect<128, OV_EPI_STORE_F32>(plan, s); break;
+      case OV_EPI_STORE_F32 * 1000 + 256: LaunchDirect<256, OV_EPI_STORE_F32>(plan, s); break;
+      case OV_EPI_ACCUM_F32 * 1000 + 128: LaunchDirect<128, OV_EPI_ACCUM_F32>(plan, s); break;
+      case OV_EPI_ACCUM_F32 * 1000 + 256: LaunchDirect<256, OV_EPI_ACCUM_F32>(plan, s); break;
+      case OV_EPI_SWIGLU_F16 * 1000 + 128: LaunchDirect<128, OV_EPI_SWIGLU_F16>(plan, s); break;
+      case OV_EPI_SWIGLU_F16 * 1000 + 256: LaunchDirect<256, OV_EPI_SWIGLU_F16>(plan, s); break;
+      case OV_EPI_QKNORM_ROPE_F16 * 1000 + 128:
+        LaunchDirect<128, OV_EPI_QKNORM_ROPE_F16>(plan, s);
+        break;
+      default: throw Error(OV_ERR_UNSUPPORTED, "no GEMM kernel for this epilogue / tile");
     }
   });
 }

@@ -60,10 +60,12 @@ size_t GemmWorkspaceBytes(int M, int N, int K, int epilogue, int sms);
 // Builds a plan.  `w_rows` is the number of rows of the (possibly stacked)
 // weight tensor w points at and b_row_offset the first row this product
 // uses, so one tensor map can cover all layers.
+// `err` is the word bounded waits report into (nullptr: the device error
+// word of ov_take_device_errors).
 void PlanGemm(GemmPlan* plan, const uint16_t* x, int64_t ldx, const uint16_t* w, int64_t w_rows,
               int b_row_offset, void* y, int64_t ldy, int M, int N, int K, int epilogue,
               const ov_epilogue_args* epilogue_args, void* workspace, size_t workspace_bytes,
-              int sms);
+              int sms, uint32_t* err = nullptr);
 
 void LaunchGemm(const GemmPlan& plan, cudaStream_t stream);
 
