@@ -110,9 +110,10 @@ typedef struct {
  * x, w are K-major with row strides ldx / in elements (multiples of 8);
  * y's row stride ldy is in elements of the output type.  `workspace`
  * (optional, may be NULL) enables a deterministic split-K for short-M
- * residual GEMMs; ov_gemm_workspace_bytes gives its size.  Its first 1024
- * bytes hold arrival counters: zero them once before the first call (every
- * call leaves them zero again); calls sharing a workspace must not overlap. */
+ * residual GEMMs: it holds one order counter per output tile
+ * (ov_gemm_workspace_bytes gives its size), the splits of a tile add into y
+ * in split order.  Zero the workspace once before its first use (every
+ * call leaves it zero again); calls sharing a workspace must not overlap. */
 int ov_gemm_f16(const uint16_t* x, size_t ldx, const uint16_t* w, void* y, size_t ldy,
                 size_t rows, size_t in, size_t out, int epilogue,
                 const ov_epilogue_args* args, void* workspace, size_t workspace_bytes,
@@ -128,14 +129,15 @@ int ov_interleave_gate_up(const uint16_t* gate_up, size_t width, size_t in, uint
  * Some callers cannot call cudaMalloc: a host process that has handed all
  * of the GPU's memory to its own pool, or code on a latency-critical path
  * where cudaMalloc / cudaFree would block on or synchronise the device.
- * This entry point allocates nothing.  Its split-K scratch is a 10 MiB
- * file-scope device array that every GPU loading the library holds until
- * the process exits; bounded waits report into a status word kept with it.
+ * This entry point allocates nothing.  Its split-K scratch (per-tile order
+ * counters) is a 64 KiB file-scope device array that every GPU loading the
+ * library holds until the process exits; bounded waits report into a status
+ * word kept with it.
  * Inputs and outputs are the caller's, as for ov_gemm_f16.
  *   - The first call on a device sets up that device (looks up the array's
  *     device address with that device current and clears its counters);
  *     make that first call before any stream capture.
- *   - Products that would need more than 10 MiB of split-K scratch are
+ *   - Products that would need more than 64 KiB of split-K scratch are
  *     rejected with OV_ERR_INVALID (none do on a 148-SM B200).
  *   - Every call shares the array, which keeps the last call's contents:
  *     calls that overlap on the GPU (different streams, or different host

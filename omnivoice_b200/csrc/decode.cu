@@ -63,6 +63,8 @@ __global__ void __launch_bounds__(kScoreWarps * 32)
                  int vocab, uint32_t mask_id, float guidance, const UttDesc* __restrict__ utts,
                  const int32_t* __restrict__ frame_utt, int single_frames,
                  int32_t* __restrict__ prediction, float* __restrict__ confidence) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int64_t item = static_cast<int64_t>(blockIdx.x) * kScoreWarps + (threadIdx.x >> 5);
   if (item >= static_cast<int64_t>(total_frames) * codebooks) return;
@@ -190,6 +192,8 @@ __global__ void __launch_bounds__(kSelectThreads)
   __shared__ int s_total;
   __shared__ uint32_t s_digit;
   __shared__ int s_remaining;
+  pdl_wait();
+  pdl_trigger();
   const int tid = threadIdx.x;
   const UttDesc d = table != nullptr ? table[blockIdx.x] : single;
   const int frames = d.frames;
@@ -319,11 +323,10 @@ void LaunchScore(const float* logits, int64_t ld, int total_frames, int codebook
   if (total_frames == 0) return;
   if (vocab > 32 * kMaxVocabPerLane) throw Error(OV_ERR_UNSUPPORTED, "vocab > 1056");
   const int64_t items = static_cast<int64_t>(total_frames) * codebooks;
-  score_kernel<<<static_cast<unsigned>((items + kScoreWarps - 1) / kScoreWarps),
-                 kScoreWarps * 32, 0, stream>>>(logits, ld, total_frames, codebooks, vocab,
-                                                mask_id, guidance, utts, frame_utt,
-                                                single_frames, prediction, confidence);
-  Check(cudaGetLastError(), "score kernel launch");
+  Launch(score_kernel, dim3(static_cast<unsigned>((items + kScoreWarps - 1) / kScoreWarps)),
+         dim3(kScoreWarps * 32), 0, stream, "score kernel launch", logits, ld, total_frames,
+         codebooks, vocab, mask_id, guidance, utts, frame_utt, single_frames, prediction,
+         confidence);
 }
 
 void ConfigureSelectKernel() {
@@ -343,11 +346,10 @@ void LaunchSelect(const int32_t* prediction, const float* confidence, int codebo
   const size_t smem = static_cast<size_t>(max_slots > 0 ? max_slots : 1) * sizeof(uint32_t);
   SetMaxDynamicSmem(reinterpret_cast<const void*>(select_kernel),
                     kMaxSlots * static_cast<int>(sizeof(uint32_t)));
-  select_kernel<<<utterances, kSelectThreads, smem, stream>>>(
-      prediction, confidence, codebooks, layer_penalty, temperature, noise_mode, mask_id, codes,
-      unmasked_at, ids, ids_rows, single, table, ctl, explicit_count, explicit_step,
-      single_cond_row, single_uncond_row, DeviceErrorWord());
-  Check(cudaGetLastError(), "select kernel launch");
+  Launch(select_kernel, dim3(utterances), dim3(kSelectThreads), smem, stream,
+         "select kernel launch", prediction, confidence, codebooks, layer_penalty, temperature,
+         noise_mode, mask_id, codes, unmasked_at, ids, ids_rows, single, table, ctl,
+         explicit_count, explicit_step, single_cond_row, single_uncond_row, DeviceErrorWord());
 }
 
 }  // namespace ovb

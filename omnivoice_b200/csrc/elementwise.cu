@@ -18,7 +18,7 @@
 namespace ovb {
 namespace {
 
-constexpr int kRowsPerBlock = 8;  // warps per block, one row each
+constexpr int kRowsPerBlock = 4;  // warps per block, one row each
 
 // Sum of squares -> 1 / sqrt(mean + eps), IEEE sqrt and division so the
 // host oracle can evaluate the same expression.
@@ -62,6 +62,8 @@ __global__ void __launch_bounds__(kRowsPerBlock * 32)
                  float* __restrict__ hidden, const float* __restrict__ norm_weight,
                  float epsilon, __half* __restrict__ normed, uint32_t* err) {
   constexpr int width = 128 * kVec;
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kRowsPerBlock + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -110,6 +112,8 @@ __global__ void __launch_bounds__(kRowsPerBlock * 32)
                    int64_t rows, const float* __restrict__ weight, __half* __restrict__ output,
                    float epsilon) {
   constexpr int width = 128 * kVec;
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kRowsPerBlock + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -211,22 +215,22 @@ void LaunchEmbed(const float* text_table, size_t text_vocab, const int32_t* row_
                  cudaStream_t stream) {
   if (rows == 0) return;
   uint32_t* err = DeviceErrorWord();
-  OV_VEC_DISPATCH(width, (embed_kernel<V><<<Blocks(rows), kRowsPerBlock * 32, 0, stream>>>(
-                              text_table, static_cast<int64_t>(text_vocab), row_text_ids,
-                              audio_table, static_cast<int64_t>(audio_vocab), ids,
-                              static_cast<int>(codebooks), static_cast<int64_t>(rows), hidden,
-                              norm_weight, epsilon, reinterpret_cast<__half*>(normed), err)));
-  Check(cudaGetLastError(), "embed kernel launch");
+  OV_VEC_DISPATCH(width, (Launch(embed_kernel<V>, dim3(Blocks(rows)), dim3(kRowsPerBlock * 32),
+                                 0, stream, "embed kernel launch", text_table,
+                                 static_cast<int64_t>(text_vocab), row_text_ids, audio_table,
+                                 static_cast<int64_t>(audio_vocab), ids,
+                                 static_cast<int>(codebooks), static_cast<int64_t>(rows), hidden,
+                                 norm_weight, epsilon, reinterpret_cast<__half*>(normed), err)));
 }
 
 void LaunchRmsNorm(const float* input, const int32_t* indices, size_t rows,
                    const float* weight, uint16_t* output, size_t width, float epsilon,
                    cudaStream_t stream) {
   if (rows == 0) return;
-  OV_VEC_DISPATCH(width, (rmsnorm_kernel<V><<<Blocks(rows), kRowsPerBlock * 32, 0, stream>>>(
-                              input, indices, static_cast<int64_t>(rows), weight,
-                              reinterpret_cast<__half*>(output), epsilon)));
-  Check(cudaGetLastError(), "rmsnorm kernel launch");
+  OV_VEC_DISPATCH(width, (Launch(rmsnorm_kernel<V>, dim3(Blocks(rows)), dim3(kRowsPerBlock * 32),
+                                 0, stream, "rmsnorm kernel launch", input, indices,
+                                 static_cast<int64_t>(rows), weight,
+                                 reinterpret_cast<__half*>(output), epsilon)));
 }
 
 }  // namespace ovb

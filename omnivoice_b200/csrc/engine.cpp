@@ -301,6 +301,22 @@ void Engine::Prepare(const ov_conditional_input* inputs, size_t count,
   }
   cu[n_seqs_] = static_cast<int32_t>(R_);
   EnsureRope(max_seqlen_);
+  // Attention work list: every (sequence, pair of 128-query tiles), longest
+  // sequences first so that the long CTAs start in the first wave.
+  std::vector<int32_t> seq_order(n_seqs_);
+  for (size_t q = 0; q < n_seqs_; ++q) seq_order[q] = static_cast<int32_t>(q);
+  std::stable_sort(seq_order.begin(), seq_order.end(), [&](int32_t a, int32_t b) {
+    return cu[a + 1] - cu[a] > cu[b + 1] - cu[b];
+  });
+  std::vector<int32_t> items;
+  for (const int32_t q : seq_order) {
+    const int32_t len = cu[q + 1] - cu[q];
+    for (int32_t pair = 0; pair * 256 < len; ++pair) {
+      items.push_back(q);
+      items.push_back(pair);
+    }
+  }
+  n_items_ = items.size() / 2;
 
   // Decoding state: per-utterance schedules, the union of non-empty steps,
   // and for the reference noise the host mt19937_64 stream of each seed.
@@ -353,6 +369,7 @@ void Engine::Prepare(const ov_conditional_input* inputs, size_t count,
   moved |= positions_.Reserve(R_);
   moved |= row_text_.Reserve(R_);
   moved |= cu_seqlens_.Reserve(n_seqs_ + 1);
+  moved |= attn_items_.Reserve(std::max<size_t>(items.size(), 2));
   moved |= targets_.Reserve(2 * total_frames_);
   moved |= frame_utt_.Reserve(total_frames_);
   moved |= utts_d_.Reserve(n);
@@ -397,7 +414,8 @@ void Engine::Prepare(const ov_conditional_input* inputs, size_t count,
       Uploader::Need(ids.size() * 4) + Uploader::Need(cu.size() * 4) +
       Uploader::Need(targets.size() * 4) + Uploader::Need(frame_utt.size() * 4) +
       Uploader::Need(n * sizeof(UttDesc)) + Uploader::Need(counts.size() * 4) +
-      Uploader::Need(step_list_.size() * 4) + Uploader::Need(gumbel.size() * 4);
+      Uploader::Need(step_list_.size() * 4) + Uploader::Need(gumbel.size() * 4) +
+      Uploader::Need(items.size() * 4);
   if (need > staging_bytes_) {
     if (staging_ != nullptr) Check(cudaFreeHost(staging_), "free staging");
     staging_ = nullptr;
@@ -412,6 +430,7 @@ void Engine::Prepare(const ov_conditional_input* inputs, size_t count,
   up.Add(row_text_, row_text);
   up.Add(ids_init_, ids);
   up.Add(cu_seqlens_, cu);
+  up.Add(attn_items_, items);
   up.Add(targets_, targets);
   up.Add(frame_utt_, frame_utt);
   up.Add(utts_d_.get(), utts_.data(), n);
@@ -497,7 +516,8 @@ void Engine::EnqueueForward(cudaStream_t s, Marker* m) {
     LaunchGemm(p.qkv, s);
     mark(kAttention, attn_flops, 0.0);
     LaunchAttention(qkv_map_, cu_seqlens_.get(), static_cast<int>(n_seqs_),
-                    static_cast<int>(max_seqlen_), static_cast<int>(cfg_.heads),
+                    static_cast<int>(max_seqlen_), attn_items_.get(),
+                    static_cast<int>(n_items_), static_cast<int>(cfg_.heads),
                     static_cast<int>(cfg_.kv_heads), scale,
                     reinterpret_cast<__half*>(attn_.get()), static_cast<int64_t>(QH_), s);
     mark(kGemmO, 2.0 * R * QH_ * H, 0.0);
@@ -579,6 +599,7 @@ std::vector<ov_kernel_time> Engine::Profile() {
   cudaGraphExec_t exec = nullptr;
   Check(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "begin capture");
   try {
+    const PdlScope no_pdl(false);  // event nodes sit between the kernels
     EnqueueForward(s, &marker);
     if (decode_ready_) EnqueueDecode(s, &marker);
     marker.Mark(-1, 0.0, 0.0);
@@ -627,6 +648,7 @@ void Engine::CaptureGraph() {
   DestroyGraph();
   Check(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), "begin capture");
   try {
+    const PdlScope pdl(true);
     EnqueueForward(stream_);
     EnqueueDecode(stream_);
   } catch (...) {
@@ -695,7 +717,10 @@ void Engine::Fetch(int32_t** codes, int32_t** unmasked_at) {
 void Engine::ForwardOnce(float* logits, float guidance, int32_t* prediction, float* confidence) {
   Activate();
   EnqueueReset(stream_);
-  EnqueueForward(stream_);
+  {
+    const PdlScope pdl(true);
+    EnqueueForward(stream_);
+  }
   const size_t F = frames_[0];
   if (prediction != nullptr) {
     LaunchScore(logits_.get(), static_cast<int64_t>(ldl_), static_cast<int>(total_frames_),

@@ -5,24 +5,36 @@
 // generator.cpp:272-300: SwiGLU (generator_kernels.hip:191-200), QK
 // RMSNorm + RoPE (:102-159) and the residual add (beta = 1).
 //
-// One CTA computes one 128 x BN tile of y, optionally over a slice of K:
+// Persistent kernel, one CTA per SM at most, looping over work units
+// (128 x BN output tiles, times the split-K factor):
 //   warp 0      TMA producer: 128x64 tiles of x and BNx64 tiles of w,
-//               128-byte swizzled, into a STAGES-deep shared-memory ring;
-//   warp 1      allocates BN tensor-memory columns and, from one thread,
-//               issues tcgen05.mma (M=128, N=BN, K=16) into them, releasing
-//               ring slots with tcgen05.commit;
-//   warps 2..5  epilogue: each thread owns one accumulator row (tensor
-//               memory lane), loads it with tcgen05.ld and applies the
-//               fused epilogue.
-// Split-K (residual epilogue only) is deterministic: every split writes
-// its partial tile to a workspace and the last split to arrive sums the
-// partials in split order before adding them to y.
+//               128-byte swizzled, into a STAGES-deep shared-memory ring
+//               that runs continuously across units;
+//   warp 1      owns 2 x BN tensor-memory columns (two accumulators) and,
+//               from one thread, issues tcgen05.mma (M=128, N=BN, K=16)
+//               into the accumulator of the current unit, releasing ring
+//               slots with tcgen05.commit;
+//   warps 2..5  epilogue: thread r owns accumulator row r (tensor-memory
+//               lane r); it loads its row with tcgen05.ld, applies the fused
+//               epilogue, writes 128-byte row pieces into a 128B-swizzled
+//               shared-memory staging tile, and one thread stores the tile
+//               with a TMA bulk store -- or, for the residual add, a TMA
+//               bulk reduce-add into y (one writer per element: exact and
+//               deterministic).  The epilogue of unit i overlaps the MMAs
+//               of unit i+1 (double-buffered accumulators).
+// Split-K (residual epilogue, short M): the splits of a tile add their
+// partial sums into y in split order, ordered by a per-tile counter, so the
+// sum order is fixed.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "gemm.hpp"
@@ -37,341 +49,464 @@ constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kThreads = 192;
 constexpr int kRingBytes = 196608;
-// Split-K workspace: arrival counters first (zero between launches), then
-// the partial tiles.
-constexpr size_t kCounterBytes = 1024;
+constexpr uint32_t kStageTile = 128 * 128;  // one staging tile: 128 rows x 128 bytes
+constexpr int kGroupM = 8;                  // rasterisation group of m tiles
 
-template <int BN>
+template <int BN, int EPI>
 struct TileConfig {
   static constexpr uint32_t kABytes = kBM * kBK * 2;
   static constexpr uint32_t kBBytes = BN * kBK * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   static constexpr int kStages = kRingBytes / kStageBytes;
-  static constexpr size_t kSmemBytes = static_cast<size_t>(kStages) * kStageBytes + 1024 + 256;
+  static constexpr uint32_t kNormFloats = EPI == OV_EPI_QKNORM_ROPE_F16 ? 256 : 0;
+  static constexpr size_t kSmemBytes =
+      static_cast<size_t>(kStages) * kStageBytes + 2 * kStageTile + kNormFloats * 4 + 1024 + 512;
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
-__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + expf(-g)) * u; }
+// silu(g) * u with the hardware exponential and a fast divide: both are
+// accurate to a few float32 ulps, far below the half rounding that follows
+// (generator_kernels.hip:196-198 computes g / (1 + exp(-g)) * u).  For
+// g < -88 the exponential overflows and __fdividef returns 0, the limit.
+__device__ __forceinline__ float silu_mul(float g, float u) {
+  return __fdividef(g, 1.0f + __expf(-g)) * u;
+}
+
+// Unit u -> (m tile, n tile, split).  Tiles are visited in groups of
+// kGroupM m tiles, all n tiles of a group before the next group, so a
+// group's activations stay in L2 while the weights stream past.
+__device__ __forceinline__ void UnitCoords(const GemmArgs& a, int u, int& m_tile, int& n_tile,
+                                           int& split) {
+  const int tile = u / a.splits;
+  split = u - tile * a.splits;
+  const int per_group = kGroupM * a.num_n;
+  const int g = tile / per_group;
+  const int first_m = g * kGroupM;
+  const int gm = min(kGroupM, a.num_m - first_m);
+  const int local = tile - g * per_group;
+  n_tile = local / gm;
+  m_tile = first_m + local % gm;
+}
+
+// Epilogue state shared by the 128 epilogue threads.
+struct EpilogueCtx {
+  uint8_t* staging;      // 2 x kStageTile, 1024-byte aligned
+  uint32_t chunk_iter;   // staging buffer alternation
+  int ep;                // 0..127
+  int row;               // tile row = tensor-memory lane
+};
+
+// Writes this thread's 128-byte row piece into the next staging tile and
+// has one thread store (or reduce-add) the tile at column x, row y0.
+template <bool kReduce>
+__device__ __forceinline__ void EmitChunk(EpilogueCtx& c, const CUtensorMap* map,
+                                          const uint32_t (&w)[32], int x, int y0) {
+  uint8_t* buf = c.staging + (c.chunk_iter & 1u) * kStageTile;
+  if (c.chunk_iter >= 2 && c.ep == 0) bulk_wait_group_read<1>();
+  named_barrier(1, 128);  // the staging tile is free again
+  uint8_t* dst = buf + c.row * 128;
+#pragma unroll
+  for (int q = 0; q < 8; ++q)
+    *reinterpret_cast<uint4*>(dst + ((q ^ (c.row & 7)) << 4)) =
+        make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+  fence_proxy_async_smem();
+  named_barrier(1, 128);
+  if (c.ep == 0) {
+    if (kReduce)
+      tma_reduce_add_2d(map, buf, x, y0);
+    else
+      tma_store_2d(map, buf, x, y0);
+    bulk_commit_group();
+  }
+  ++c.chunk_iter;
+}
 
 template <int BN, int EPI>
-__device__ __forceinline__ void epilogue(const GemmArgs& a, uint32_t tmem, int m_tile, int n_tile,
-                                         int split, int* flag) {
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int quarter = warp & 3;  // tensor memory lanes 32*quarter .. +31
-  const int row_local = quarter * 32 + lane;
-  const int64_t grow = static_cast<int64_t>(m_tile) * kBM + row_local;
-  const bool row_ok = grow < a.M;
-  const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-
+__device__ __forceinline__ void EpilogueUnit(const GemmArgs& a, const CUtensorMap* map_y,
+                                             EpilogueCtx& c, uint32_t tacc, int m_tile,
+                                             int n_tile, const float* norm_w) {
+  const int y0 = m_tile * kBM;
   if constexpr (EPI == OV_EPI_STORE_F32 || EPI == OV_EPI_ACCUM_F32) {
-    if (EPI == OV_EPI_ACCUM_F32 && a.splits > 1) {
-      const int tile = m_tile * gridDim.x + n_tile;
-      float* part_base = a.partials + static_cast<int64_t>(tile) * a.splits * (kBM * BN);
-      float* mine = part_base + static_cast<int64_t>(split) * (kBM * BN) + row_local * BN;
-#pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(trow + c0, r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int j = 0; j < 32; j += 4)
-          __stcg(reinterpret_cast<float4*>(mine + c0 + j),
-                 make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                             __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3])));
-      }
-      __threadfence();
-      named_barrier(1, 128);
-      if (threadIdx.x == 64) {
-        const uint32_t prev = atomicAdd(a.counters + tile, 1u);
-        *flag = prev == static_cast<uint32_t>(a.splits - 1) ? 1 : 0;
-      }
-      named_barrier(1, 128);
-      if (*flag == 0) return;
-      __threadfence();
-      if (row_ok) {
-        float* y = static_cast<float*>(a.y) + grow * a.ldy + n_tile * BN;
-        const float* rowp = part_base + row_local * BN;
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 4) {
-          if (n_tile * BN + c >= a.N) break;
-          float4 acc = __ldcg(reinterpret_cast<const float4*>(rowp + c));
-          for (int s = 1; s < a.splits; ++s) {
-            const float4 p =
-                __ldcg(reinterpret_cast<const float4*>(rowp + static_cast<int64_t>(s) * kBM * BN + c));
-            acc.x += p.x;
-            acc.y += p.y;
-            acc.z += p.z;
-            acc.w += p.w;
-          }
-          float4 old = *reinterpret_cast<const float4*>(y + c);
-          old.x += acc.x;
-          old.y += acc.y;
-          old.z += acc.z;
-          old.w += acc.w;
-          *reinterpret_cast<float4*>(y + c) = old;
-        }
-      }
-      if (threadIdx.x == 64) a.counters[tile] = 0u;
-      return;
-    }
 #pragma unroll 1
     for (int c0 = 0; c0 < BN; c0 += 32) {
+      const int x = n_tile * BN + c0;
+      if (x >= a.out_cols) break;  // uniform over the epilogue threads
       uint32_t r[32];
-      tmem_ld_32x32b_x32(trow + c0, r);
+      tmem_ld_32x32b_x32(tacc + c0, r);
       tmem_ld_wait();
-      const int gcol = n_tile * BN + c0;
-      if (row_ok) {
-        float* y = static_cast<float*>(a.y) + grow * a.ldy + gcol;
-#pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-          if (gcol + j < a.N) {
-            float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                                   __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
-            if (EPI == OV_EPI_ACCUM_F32) {
-              const float4 old = *reinterpret_cast<const float4*>(y + j);
-              v.x = old.x + v.x;
-              v.y = old.y + v.y;
-              v.z = old.z + v.z;
-              v.w = old.w + v.w;
-            }
-            *reinterpret_cast<float4*>(y + j) = v;
-          }
-        }
-      }
+      EmitChunk<EPI == OV_EPI_ACCUM_F32>(c, map_y, r, x, y0);
     }
   } else if constexpr (EPI == OV_EPI_SWIGLU_F16) {
-    // The tile holds BN / 128 groups of [64 gate | 64 up] columns.
+    // The tile holds BN / 128 groups of [64 gate | 64 up] columns; each
+    // group gives 64 half outputs = one 128-byte row piece.
     constexpr int G = OV_SWIGLU_GROUP;
 #pragma unroll 1
     for (int gi = 0; gi < BN / (2 * G); ++gi) {
-#pragma unroll 1
-      for (int c0 = 0; c0 < G; c0 += 32) {
-        uint32_t g[32], u[32];
-        tmem_ld_32x32b_x32(trow + gi * 2 * G + c0, g);
-        tmem_ld_32x32b_x32(trow + gi * 2 * G + G + c0, u);
-        tmem_ld_wait();
-        if (row_ok) {
-          __half* y = static_cast<__half*>(a.y) + grow * a.ldy + n_tile * (BN / 2) + gi * G + c0;
+      uint32_t out[32];
 #pragma unroll
-          for (int j = 0; j < 32; j += 8) {
-            uint4 packed;
-            packed.x = pack_half2(silu_mul(__uint_as_float(g[j]), __uint_as_float(u[j])),
-                                  silu_mul(__uint_as_float(g[j + 1]), __uint_as_float(u[j + 1])));
-            packed.y = pack_half2(silu_mul(__uint_as_float(g[j + 2]), __uint_as_float(u[j + 2])),
-                                  silu_mul(__uint_as_float(g[j + 3]), __uint_as_float(u[j + 3])));
-            packed.z = pack_half2(silu_mul(__uint_as_float(g[j + 4]), __uint_as_float(u[j + 4])),
-                                  silu_mul(__uint_as_float(g[j + 5]), __uint_as_float(u[j + 5])));
-            packed.w = pack_half2(silu_mul(__uint_as_float(g[j + 6]), __uint_as_float(u[j + 6])),
-                                  silu_mul(__uint_as_float(g[j + 7]), __uint_as_float(u[j + 7])));
-            *reinterpret_cast<uint4*>(y + j) = packed;
-          }
-        }
+      for (int h = 0; h < 2; ++h) {
+        uint32_t g[32], u[32];
+        tmem_ld_32x32b_x32(tacc + gi * 2 * G + h * 32, g);
+        tmem_ld_32x32b_x32(tacc + gi * 2 * G + G + h * 32, u);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; j += 2)
+          out[h * 16 + j / 2] =
+              pack_half2(silu_mul(__uint_as_float(g[j]), __uint_as_float(u[j])),
+                         silu_mul(__uint_as_float(g[j + 1]), __uint_as_float(u[j + 1])));
       }
+      EmitChunk<false>(c, map_y, out, n_tile * (BN / 2) + gi * G, y0);
     }
   } else if constexpr (EPI == OV_EPI_QKNORM_ROPE_F16) {
     static_assert(BN == 128, "one head of 128 per tile");
     float v[128];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
+    for (int q = 0; q < 4; ++q) {
       uint32_t r[32];
-      tmem_ld_32x32b_x32(trow + c * 32, r);
+      tmem_ld_32x32b_x32(tacc + q * 32, r);
       tmem_ld_wait();
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[c * 32 + j] = __uint_as_float(r[j]);
+      for (int j = 0; j < 32; ++j) v[q * 32 + j] = __uint_as_float(r[j]);
     }
-    if (!row_ok) return;
     const int slot = n_tile;
-    __half* y = static_cast<__half*>(a.y) + grow * a.ldy + slot * 128;
+    uint32_t lo[32], hi[32];
     if (slot < a.heads + a.kv_heads) {
-      const float* w = slot < a.heads ? a.q_norm : a.k_norm;
+      const float* w = norm_w + (slot < a.heads ? 0 : 128);
       float ss = 0.0f;
 #pragma unroll
       for (int j = 0; j < 128; ++j) ss = fmaf(v[j], v[j], ss);
       const float scale = 1.0f / sqrtf(ss / 128.0f + a.epsilon);
-      int pos = a.positions[grow];
+      const int64_t grow = static_cast<int64_t>(y0) + c.row;
+      int pos = grow < a.M ? a.positions[grow] : 0;
       if (pos < 0 || pos >= a.max_positions) {
         atomicOr(a.err, kErrBadArgument);
         pos = 0;
       }
-      const float* cs = a.rope_cos + static_cast<int64_t>(pos) * 64;
-      const float* sn = a.rope_sin + static_cast<int64_t>(pos) * 64;
+      const float4* cs = reinterpret_cast<const float4*>(a.rope_cos + static_cast<int64_t>(pos) * 64);
+      const float4* sn = reinterpret_cast<const float4*>(a.rope_sin + static_cast<int64_t>(pos) * 64);
 #pragma unroll
-      for (int i0 = 0; i0 < 64; i0 += 8) {
-        float lo[8], hi[8];
+      for (int i4 = 0; i4 < 16; ++i4) {
+        const float4 c4 = __ldg(cs + i4);
+        const float4 s4 = __ldg(sn + i4);
+        const float cc[4] = {c4.x, c4.y, c4.z, c4.w};
+        const float ssn[4] = {s4.x, s4.y, s4.z, s4.w};
+        float l4[4], h4[4];
 #pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          const int i = i0 + t;
+        for (int t = 0; t < 4; ++t) {
+          const int i = i4 * 4 + t;
           const float x1 = w[i] * (v[i] * scale);
           const float x2 = w[i + 64] * (v[i + 64] * scale);
-          const float c = cs[i];
-          const float s = sn[i];
-          lo[t] = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
-          hi[t] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+          l4[t] = __fsub_rn(__fmul_rn(x1, cc[t]), __fmul_rn(x2, ssn[t]));
+          h4[t] = __fadd_rn(__fmul_rn(x2, cc[t]), __fmul_rn(x1, ssn[t]));
         }
-        uint4 p0, p1;
-        p0.x = pack_half2(lo[0], lo[1]);
-        p0.y = pack_half2(lo[2], lo[3]);
-        p0.z = pack_half2(lo[4], lo[5]);
-        p0.w = pack_half2(lo[6], lo[7]);
-        p1.x = pack_half2(hi[0], hi[1]);
-        p1.y = pack_half2(hi[2], hi[3]);
-        p1.z = pack_half2(hi[4], hi[5]);
-        p1.w = pack_half2(hi[6], hi[7]);
-        *reinterpret_cast<uint4*>(y + i0) = p0;
-        *reinterpret_cast<uint4*>(y + 64 + i0) = p1;
+        lo[i4 * 2] = pack_half2(l4[0], l4[1]);
+        lo[i4 * 2 + 1] = pack_half2(l4[2], l4[3]);
+        hi[i4 * 2] = pack_half2(h4[0], h4[1]);
+        hi[i4 * 2 + 1] = pack_half2(h4[2], h4[3]);
       }
     } else {
 #pragma unroll
-      for (int j = 0; j < 128; j += 8) {
-        uint4 p;
-        p.x = pack_half2(v[j], v[j + 1]);
-        p.y = pack_half2(v[j + 2], v[j + 3]);
-        p.z = pack_half2(v[j + 4], v[j + 5]);
-        p.w = pack_half2(v[j + 6], v[j + 7]);
-        *reinterpret_cast<uint4*>(y + j) = p;
+      for (int j = 0; j < 32; ++j) {
+        lo[j] = pack_half2(v[2 * j], v[2 * j + 1]);
+        hi[j] = pack_half2(v[64 + 2 * j], v[64 + 2 * j + 1]);
       }
     }
+    EmitChunk<false>(c, map_y, lo, slot * 128, y0);
+    EmitChunk<false>(c, map_y, hi, slot * 128 + 64, y0);
   }
 }
+
+#ifdef OV_GEMM_TRACE
+// Timing probe of a diagnostic build: %globaltimer at pipeline milestones
+// per CTA (compiled only with -DOV_GEMM_TRACE).
+__device__ unsigned long long g_gemm_trace[1024 * 16];
+#define OV_TRACE(slot) g_gemm_trace[blockIdx.x * 16 + (slot)] = global_timer_ns()
+#else
+#define OV_TRACE(slot) \
+  do {                 \
+  } while (0)
+#endif
 
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                const GemmArgs args) {
-  using Cfg = TileConfig<BN>;
+                const __grid_constant__ CUtensorMap map_y, const GemmArgs args) {
+  using Cfg = TileConfig<BN, EPI>;
   constexpr int kStages = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sa = smem;
-  uint8_t* sb = smem + kStages * Cfg::kABytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sb + kStages * Cfg::kBBytes);
+  uint8_t* sb = sa + kStages * Cfg::kABytes;
+  uint8_t* staging = sb + kStages * Cfg::kBBytes;  // 1024-byte aligned
+  float* norm_w = reinterpret_cast<float*>(staging + 2 * kStageTile);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(norm_w) + Cfg::kNormFloats * 4);
+  uint64_t* full = bars;
   uint64_t* empty = full + kStages;
-  uint64_t* done = empty + kStages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
-  int* flag = reinterpret_cast<int*>(tmem_slot + 1);
+  uint64_t* tfull = empty + kStages;  // [2]
+  uint64_t* tempty = tfull + 2;       // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int n_tile = blockIdx.x;
-  const int m_tile = blockIdx.y;
-  const int split = blockIdx.z;
-  const int kb0 = split * args.kblocks / args.splits;
-  const int kb1 = (split + 1) * args.kblocks / args.splits;
-  const int nk = kb1 - kb0;
+  if (threadIdx.x == 0) OV_TRACE(0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(done, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 128);
+    }
     fence_mbar_init();
     tma_prefetch_map(&map_a);
     tma_prefetch_map(&map_b);
+    tma_prefetch_map(&map_y);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, BN);
+    tmem_alloc(tmem_slot, 2 * BN);
     tmem_relinquish();
+  }
+  if constexpr (EPI == OV_EPI_QKNORM_ROPE_F16) {
+    if (warp >= 2) {
+      const int i = threadIdx.x - 64;
+      norm_w[i] = args.q_norm[i];
+      norm_w[128 + i] = args.k_norm[i];
+    }
   }
   tc_fence_before_sync();
   __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) OV_TRACE(1);
+  if (!(warp == 0 && lane == 0)) {
+    pdl_wait();  // inputs of the previous kernel in the stream are ready
+    pdl_trigger();
+  }
 
   if (warp == 0) {
     if (lane == 0) {
-      int issued = 0;
-      for (int i = 0; i < nk; ++i) {
-        const int s = i % kStages;
-        const uint32_t phase = static_cast<uint32_t>(i / kStages) & 1u;
-        if (i >= kStages && !mbar_wait(&empty[s], phase ^ 1u, args.err)) break;
-        mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
-        tma_load_2d(sa + s * Cfg::kABytes, &map_a, &full[s], (kb0 + i) * kBK, m_tile * kBM);
-        tma_load_2d(sb + s * Cfg::kBBytes, &map_b, &full[s], (kb0 + i) * kBK,
-                    args.b_row_offset + n_tile * BN);
-        ++issued;
+      // The weights do not depend on the previous kernel: start the weight
+      // tiles of the first ring slots before waiting for it.
+      uint32_t pre = 0;
+      if (static_cast<int>(blockIdx.x) < args.units) {
+        int m_tile, n_tile, split;
+        UnitCoords(args, blockIdx.x, m_tile, n_tile, split);
+        const int kb0 = split * args.kblocks / args.splits;
+        const int kb1 = (split + 1) * args.kblocks / args.splits;
+        pre = static_cast<uint32_t>(min(kStages, kb1 - kb0));
+        for (uint32_t i = 0; i < pre; ++i) {
+          mbar_arrive_expect_tx(&full[i], Cfg::kStageBytes);
+          tma_load_2d(sb + i * Cfg::kBBytes, &map_b, &full[i], (kb0 + static_cast<int>(i)) * kBK,
+                      args.b_row_offset + n_tile * BN);
+        }
       }
+      pdl_wait();
+      pdl_trigger();
+      OV_TRACE(2);
+      uint32_t k_iter = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < args.units; u += gridDim.x) {
+        int m_tile, n_tile, split;
+        UnitCoords(args, u, m_tile, n_tile, split);
+        const int kb0 = split * args.kblocks / args.splits;
+        const int kb1 = (split + 1) * args.kblocks / args.splits;
+        for (int kb = kb0; kb < kb1; ++kb, ++k_iter) {
+          const int s = static_cast<int>(k_iter % kStages);
+          const uint32_t phase = (k_iter / kStages) & 1u;
+          if (k_iter < pre) {  // weight tile already on its way
+            tma_load_2d(sa + s * Cfg::kABytes, &map_a, &full[s], kb * kBK, m_tile * kBM);
+            continue;
+          }
+          if (k_iter >= static_cast<uint32_t>(kStages) &&
+              !mbar_wait(&empty[s], phase ^ 1u, args.err)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
+          tma_load_2d(sa + s * Cfg::kABytes, &map_a, &full[s], kb * kBK, m_tile * kBM);
+          tma_load_2d(sb + s * Cfg::kBBytes, &map_b, &full[s], kb * kBK,
+                      args.b_row_offset + n_tile * BN);
+        }
+      }
+      OV_TRACE(10);
       // Let the copies this thread started land before the CTA can exit.
-      for (int i = std::max(0, issued - kStages); i < issued; ++i)
-        (void)mbar_wait(&full[i % kStages], static_cast<uint32_t>(i / kStages) & 1u, args.err);
+      const uint32_t first = k_iter > static_cast<uint32_t>(kStages) ? k_iter - kStages : 0u;
+      for (uint32_t i = first; i < k_iter; ++i)
+        (void)mbar_wait(&full[i % kStages], (i / kStages) & 1u, args.err);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_f16_f32(kBM, BN);
-      for (int i = 0; i < nk; ++i) {
-        const int s = i % kStages;
-        const uint32_t phase = static_cast<uint32_t>(i / kStages) & 1u;
-        if (!mbar_wait(&full[s], phase, args.err)) break;
+      uint32_t k_iter = 0;
+      int acc_iter = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < args.units; u += gridDim.x, ++acc_iter) {
+        int m_tile, n_tile, split;
+        UnitCoords(args, u, m_tile, n_tile, split);
+        const int kb0 = split * args.kblocks / args.splits;
+        const int kb1 = (split + 1) * args.kblocks / args.splits;
+        const int buf = acc_iter & 1;
+        if (acc_iter >= 2 &&
+            !mbar_wait(&tempty[buf], static_cast<uint32_t>((acc_iter >> 1) - 1) & 1u, args.err)) {
+          ok = false;
+          break;
+        }
         tc_fence_after_sync();
-        const uint32_t a0 = smem_u32(sa + s * Cfg::kABytes);
-        const uint32_t b0 = smem_u32(sb + s * Cfg::kBBytes);
+        const uint32_t d = tmem + static_cast<uint32_t>(buf * BN);
+        for (int kb = kb0; kb < kb1; ++kb, ++k_iter) {
+          const int s = static_cast<int>(k_iter % kStages);
+          const uint32_t phase = (k_iter / kStages) & 1u;
+          if (!mbar_wait(&full[s], phase, args.err)) {
+            ok = false;
+            break;
+          }
+          if (k_iter == 0) OV_TRACE(3);
+          tc_fence_after_sync();
+          const uint32_t a0 = smem_u32(sa + s * Cfg::kABytes);
+          const uint32_t b0 = smem_u32(sb + s * Cfg::kBBytes);
 #pragma unroll
-        for (int k = 0; k < kBK / 16; ++k)
-          umma_f16_ss(tmem, smem_desc_sw128(a0 + k * 32, 16, 1024),
-                      smem_desc_sw128(b0 + k * 32, 16, 1024), idesc,
-                      (i > 0 || k > 0) ? 1u : 0u);
-        umma_commit(&empty[s]);
+          for (int k = 0; k < kBK / 16; ++k)
+            umma_f16_ss(d, smem_desc_sw128(a0 + k * 32, 16, 1024),
+                        smem_desc_sw128(b0 + k * 32, 16, 1024), idesc,
+                        (kb > kb0 || k > 0) ? 1u : 0u);
+          umma_commit(&empty[s]);
+        }
+        umma_commit(&tfull[buf]);
+        if (acc_iter == 0) OV_TRACE(4);
       }
-      umma_commit(done);
+      OV_TRACE(11);
     }
   } else {
-    // Every epilogue thread runs the epilogue even after a timed-out wait
-    // (the error word is set) so the 128 threads stay in step for the
-    // split-K named barrier.
-    (void)mbar_wait(done, 0, args.err);
-    tc_fence_after_sync();
-    epilogue<BN, EPI>(args, tmem, m_tile, n_tile, split, flag);
+    EpilogueCtx c;
+    c.staging = staging;
+    c.chunk_iter = 0;
+    c.ep = threadIdx.x - 64;
+    const int quarter = warp & 3;  // tensor-memory lanes 32*quarter .. +31
+    c.row = quarter * 32 + lane;
+    int acc_iter = 0;
+    for (int u = blockIdx.x; u < args.units; u += gridDim.x, ++acc_iter) {
+      int m_tile, n_tile, split;
+      UnitCoords(args, u, m_tile, n_tile, split);
+      const int buf = acc_iter & 1;
+      // Every epilogue thread runs the epilogue even after a timed-out wait
+      // (the error word is set) so the 128 threads stay in step.
+      (void)mbar_wait(&tfull[buf], static_cast<uint32_t>(acc_iter >> 1) & 1u, args.err);
+      __syncwarp();  // the tensor-memory loads below are warp-collective
+      if (acc_iter == 0 && c.ep == 0) OV_TRACE(5);
+      tc_fence_after_sync();
+      const int tile = u / args.splits;
+      if (EPI == OV_EPI_ACCUM_F32 && args.splits > 1 && c.ep == 0) {
+        // Earlier splits of this tile first; their adds are complete.
+        (void)wait_counter_equals(args.counters + tile, static_cast<uint32_t>(split), args.err);
+        fence_proxy_async_global();
+        if (acc_iter == 0) OV_TRACE(12);
+      }
+      const uint32_t tacc =
+          tmem + static_cast<uint32_t>(buf * BN) + (static_cast<uint32_t>(quarter * 32) << 16);
+      EpilogueUnit<BN, EPI>(args, &map_y, c, tacc, m_tile, n_tile, norm_w);
+      tc_fence_before_sync();
+      mbar_arrive(&tempty[buf]);
+      if (EPI == OV_EPI_ACCUM_F32 && args.splits > 1 && c.ep == 0) {
+        bulk_wait_group<0>();
+        fence_proxy_async_global();
+        __threadfence();
+        if (split == args.splits - 1)
+          st_relaxed_gpu(args.counters + tile, 0u);  // ready for the next launch
+        else
+          red_release_gpu_add(args.counters + tile, 1u);
+      }
+      if (acc_iter == 0 && c.ep == 0) OV_TRACE(6);
+    }
+    if (c.ep == 0) bulk_wait_group<0>();
+#ifdef OV_GEMM_TRACE
+    if (c.ep == 0) {
+      OV_TRACE(7);
+      uint32_t smid;
+      asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+      g_gemm_trace[blockIdx.x * 16 + 9] = static_cast<unsigned long long>(acc_iter);
+      g_gemm_trace[blockIdx.x * 16 + 13] = smid;
+    }
+#endif
   }
   tc_fence_before_sync();
   __syncthreads();
+  if (threadIdx.x == 0) OV_TRACE(8);
   if (warp == 1) {
     tc_fence_after_sync();
-    tmem_dealloc(tmem, BN);
+    tmem_dealloc(tmem, 2 * BN);
   }
 }
 
+// Every compiled (tile width, epilogue) pair.
+#define OV_GEMM_INSTANCES(X)           \
+  X(64, OV_EPI_STORE_F32)              \
+  X(128, OV_EPI_STORE_F32)             \
+  X(256, OV_EPI_STORE_F32)             \
+  X(64, OV_EPI_ACCUM_F32)              \
+  X(128, OV_EPI_ACCUM_F32)             \
+  X(256, OV_EPI_ACCUM_F32)             \
+  X(128, OV_EPI_SWIGLU_F16)            \
+  X(256, OV_EPI_SWIGLU_F16)            \
+  X(128, OV_EPI_QKNORM_ROPE_F16)
+
 template <int BN, int EPI>
 void LaunchTyped(const GemmPlan& p, cudaStream_t stream) {
-  auto kernel = gemm_kernel<BN, EPI>;
-  SetMaxDynamicSmem(reinterpret_cast<const void*>(kernel),
-                    static_cast<int>(TileConfig<BN>::kSmemBytes));
-  kernel<<<p.grid, kThreads, TileConfig<BN>::kSmemBytes, stream>>>(p.map_a, p.map_b, p.args);
-  Check(cudaGetLastError(), "gemm kernel launch");
+  Launch(gemm_kernel<BN, EPI>, p.grid, dim3(kThreads), TileConfig<BN, EPI>::kSmemBytes, stream,
+         "gemm kernel launch", p.map_a, p.map_b, p.map_y, p.args);
 }
 
 int Tiles(int M, int N, int bn) { return ((M + kBM - 1) / kBM) * ((N + bn - 1) / bn); }
 
+bool ValidShape(int bn, int splits, int N, int K, int epilogue) {
+  if (splits < 1 || splits > 8) return false;
+  if (splits > 1 && (epilogue != OV_EPI_ACCUM_F32 || (K / kBK) / splits < 2)) return false;
+  switch (epilogue) {
+    case OV_EPI_QKNORM_ROPE_F16: return bn == 128;
+    case OV_EPI_SWIGLU_F16: return (bn == 128 || bn == 256) && N % bn == 0;
+    default: return bn == 64 || bn == 128 || bn == 256;
+  }
+}
+
 }  // namespace
 
 GemmShapeChoice ChooseGemmShape(int M, int N, int K, int epilogue, bool have_workspace, int sms) {
-  GemmShapeChoice c{128, 1};
-  if (epilogue == OV_EPI_QKNORM_ROPE_F16) return c;
-  // Time of a tile is proportional to its width; a wave is `sms` tiles.
-  // A 256-wide tile runs the tensor pipe at full rate; a 128-wide one
-  // loses a little to operand reads (weight 1.1 per column).
-  auto cost = [&](int bn) {
-    const int waves = (Tiles(M, N, bn) + sms - 1) / sms;
-    return waves * bn * (bn == 128 ? 1.1 : 1.0);
-  };
-  const bool can256 = epilogue != OV_EPI_SWIGLU_F16 || N % 256 == 0;
-  if (can256 && cost(256) <= cost(128)) c.bn = 256;
-  if (epilogue == OV_EPI_ACCUM_F32 && have_workspace) {
-    c.bn = 128;
-    const int tiles = Tiles(M, N, 128);
-    const int kblocks = K / kBK;
-    int splits = 1;
-    while (splits < 8 && tiles * (splits + 1) <= sms && kblocks / (splits + 1) >= 4) ++splits;
-    c.splits = splits;
+  if (const char* env = std::getenv("OV_GEMM_TILE")) {
+    int bn = 0, splits = 1;
+    if (std::sscanf(env, "%dx%d", &bn, &splits) >= 1 &&
+        ValidShape(bn, splits, N, K, epilogue) && (splits == 1 || have_workspace))
+      return {bn, splits};
   }
-  return c;
+  // Cost in units of (one 64-wide k block of a 128 x 64 tile): a unit of
+  // width bn over kb k blocks costs kb * bn / 64 * eff(bn) + fill, a
+  // persistent CTA runs ceil(units / sms) units one after another, and
+  // each extra split waits for the previous split's add (~ one chunk).
+  const int kblocks = K / kBK;
+  auto eff = [](int bn) { return bn == 64 ? 1.35 : bn == 128 ? 1.08 : 1.0; };
+  GemmShapeChoice best{128, 1};
+  double best_cost = 1e300;
+  for (int bn : {64, 128, 256}) {
+    for (int s = 1; s <= 4; ++s) {
+      if (!ValidShape(bn, s, N, K, epilogue) || (s > 1 && !have_workspace)) continue;
+      const double units = static_cast<double>(Tiles(M, N, bn)) * s;
+      const double rounds = std::ceil(units / sms);
+      const double per_unit = (static_cast<double>(kblocks) / s) * (bn / 64.0) * eff(bn) + 4.0;
+      const double cost = rounds * per_unit + (s - 1) * 3.0;
+      if (cost < best_cost - 1e-9) {
+        best_cost = cost;
+        best = {bn, s};
+      }
+    }
+  }
+  return best;
 }
 
 size_t GemmWorkspaceBytes(int M, int N, int K, int epilogue, int sms) {
   const GemmShapeChoice c = ChooseGemmShape(M, N, K, epilogue, true, sms);
   if (c.splits <= 1) return 0;
-  const size_t tiles = static_cast<size_t>(Tiles(M, N, c.bn));
-  return kCounterBytes + tiles * c.splits * kBM * c.bn * sizeof(float);
+  return static_cast<size_t>(Tiles(M, N, c.bn)) * sizeof(uint32_t);
 }
 
 void PlanGemm(GemmPlan* plan, const uint16_t* x, int64_t ldx, const uint16_t* w, int64_t w_rows,
@@ -383,18 +518,18 @@ void PlanGemm(GemmPlan* plan, const uint16_t* x, int64_t ldx, const uint16_t* w,
   OV_REQUIRE(ldx % 8 == 0 && ldx >= K, "x row stride must be a multiple of 8 and >= K");
   OV_REQUIRE(epilogue >= OV_EPI_STORE_F32 && epilogue <= OV_EPI_QKNORM_ROPE_F16, "epilogue");
   const bool half_out = epilogue == OV_EPI_SWIGLU_F16 || epilogue == OV_EPI_QKNORM_ROPE_F16;
-  OV_REQUIRE(ldy % (half_out ? 8 : 4) == 0, "y row stride must allow 16-byte vector stores");
+  OV_REQUIRE(ldy % (half_out ? 8 : 4) == 0, "y row stride must be a multiple of 16 bytes");
   OV_REQUIRE((reinterpret_cast<uintptr_t>(y) & 15u) == 0, "y must be 16-byte aligned");
   GemmShapeChoice choice =
       ChooseGemmShape(M, N, K, epilogue, workspace != nullptr && workspace_bytes > 0, sms);
-  if (choice.splits > 1) {
-    const size_t need = GemmWorkspaceBytes(M, N, K, epilogue, sms);
-    if (workspace_bytes < need) choice.splits = 1;
-  }
+  if (choice.splits > 1 &&
+      workspace_bytes < static_cast<size_t>(Tiles(M, N, choice.bn)) * sizeof(uint32_t))
+    choice = ChooseGemmShape(M, N, K, epilogue, false, sms);
+  int out_cols = N;
   if (epilogue == OV_EPI_SWIGLU_F16) {
-    OV_REQUIRE(N % 128 == 0 && N % choice.bn == 0,
-               "SwiGLU output features must be a multiple of 128");
-    OV_REQUIRE(ldy >= N / 2, "y row stride");
+    OV_REQUIRE(N % 128 == 0, "SwiGLU output features must be a multiple of 128");
+    out_cols = N / 2;
+    OV_REQUIRE(ldy >= out_cols, "y row stride");
   } else if (epilogue == OV_EPI_QKNORM_ROPE_F16) {
     OV_REQUIRE(ea != nullptr && ea->head_dim == 128, "QK-norm epilogue needs head_dim 128");
     OV_REQUIRE(N == (ea->heads + 2 * ea->kv_heads) * 128, "QKV width");
@@ -414,17 +549,12 @@ void PlanGemm(GemmPlan* plan, const uint16_t* x, int64_t ldx, const uint16_t* w,
   a.kblocks = K / kBK;
   a.splits = choice.splits;
   a.b_row_offset = b_row_offset;
-  a.ldy = ldy;
-  a.y = y;
+  a.num_m = (M + kBM - 1) / kBM;
+  a.num_n = (N + choice.bn - 1) / choice.bn;
+  a.units = a.num_m * a.num_n * a.splits;
+  a.out_cols = out_cols;
   a.err = err != nullptr ? err : DeviceErrorWord();
-  if (choice.splits > 1) {
-    // Counters live at a fixed place, ahead of the partial tiles, so a
-    // workspace shared by products of different shapes keeps them zero
-    // (every split-K launch leaves its counters at zero).
-    OV_REQUIRE(Tiles(M, N, choice.bn) * sizeof(uint32_t) <= kCounterBytes, "split-K tile count");
-    a.counters = static_cast<uint32_t*>(workspace);
-    a.partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterBytes);
-  }
+  if (choice.splits > 1) a.counters = static_cast<uint32_t*>(workspace);
   if (ea != nullptr) {
     a.q_norm = ea->q_norm;
     a.k_norm = ea->k_norm;
@@ -442,40 +572,47 @@ void PlanGemm(GemmPlan* plan, const uint16_t* x, int64_t ldx, const uint16_t* w,
   EncodeTensorMap2D(&plan->map_b, w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, static_cast<uint64_t>(K),
                     static_cast<uint64_t>(w_rows), static_cast<uint64_t>(K) * 2, kBK,
                     static_cast<uint32_t>(choice.bn), CU_TENSOR_MAP_SWIZZLE_128B);
-  plan->grid = dim3(static_cast<unsigned>((N + choice.bn - 1) / choice.bn),
-                    static_cast<unsigned>((M + kBM - 1) / kBM),
-                    static_cast<unsigned>(choice.splits));
-  plan->smem_bytes = choice.bn == 256 ? TileConfig<256>::kSmemBytes : TileConfig<128>::kSmemBytes;
+  // y: 128-byte row pieces (32 floats or 64 halves) x 128 rows per box.
+  if (half_out)
+    EncodeTensorMap2D(&plan->map_y, y, CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                      static_cast<uint64_t>(out_cols), static_cast<uint64_t>(M),
+                      static_cast<uint64_t>(ldy) * 2, 64, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
+  else
+    EncodeTensorMap2D(&plan->map_y, y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                      static_cast<uint64_t>(out_cols), static_cast<uint64_t>(M),
+                      static_cast<uint64_t>(ldy) * 4, 32, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
+  // With split-K every round of the persistent grid holds whole tiles, so a
+  // split only waits for lower-numbered CTAs of its own round.
+  int grid = std::min(a.units, sms);
+  if (a.splits > 1) grid = std::max(a.splits, grid / a.splits * a.splits);
+  plan->grid = dim3(static_cast<unsigned>(grid), 1, 1);
+  switch (epilogue * 1000 + choice.bn) {
+#define OV_SMEM_CASE(BN, EPI) \
+  case EPI * 1000 + BN: plan->smem_bytes = TileConfig<BN, EPI>::kSmemBytes; break;
+    OV_GEMM_INSTANCES(OV_SMEM_CASE)
+#undef OV_SMEM_CASE
+    default: throw Error(OV_ERR_UNSUPPORTED, "no GEMM kernel for this epilogue / tile");
+  }
 }
 
 void ConfigureGemmKernels() {
-  SetMaxDynamicSmem(reinterpret_cast<const void*>(gemm_kernel<128, OV_EPI_STORE_F32>),
-                    static_cast<int>(TileConfig<128>::kSmemBytes));
-  SetMaxDynamicSmem(reinterpret_cast<const void*>(gemm_kernel<256, OV_EPI_STORE_F32>),
-                    static_cast<int>(TileConfig<256>::kSmemBytes));
-  SetMaxDynamicSmem(reinterpret_cast<const void*>(gemm_kernel<128, OV_EPI_ACCUM_F32>),
-                    static_cast<int>(TileConfig<128>::kSmemBytes));
-  SetMaxDynamicSmem(reinterpret_cast<const void*>(gemm_kernel<256, OV_EPI_ACCUM_F32>),
-                    static_cast<int>(TileConfig<256>::kSmemBytes));
-  SetMaxDynamicSmem(reinterpret_cast<const void*>(gemm_kernel<128, OV_EPI_SWIGLU_F16>),
-                    static_cast<int>(TileConfig<128>::kSmemBytes));
-  SetMaxDynamicSmem(reinterpret_cast<const void*>(gemm_kernel<256, OV_EPI_SWIGLU_F16>),
-                    static_cast<int>(TileConfig<256>::kSmemBytes));
-  SetMaxDynamicSmem(reinterpret_cast<const void*>(gemm_kernel<128, OV_EPI_QKNORM_ROPE_F16>),
-                    static_cast<int>(TileConfig<128>::kSmemBytes));
+#define OV_CONFIGURE(BN, EPI)                                                   \
+  SetMaxDynamicSmem(reinterpret_cast<const void*>(gemm_kernel<BN, EPI>),        \
+                    static_cast<int>(TileConfig<BN, EPI>::kSmemBytes));
+  OV_GEMM_INSTANCES(OV_CONFIGURE)
+#undef OV_CONFIGURE
 }
 
 void LaunchGemm(const GemmPlan& p, cudaStream_t stream) {
   switch (p.epilogue * 1000 + p.bn) {
-    case OV_EPI_STORE_F32 * 1000 + 128: LaunchTyped<128, OV_EPI_STORE_F32>(p, stream); break;
-    case OV_EPI_STORE_F32 * 1000 + 256: LaunchTyped<256, OV_EPI_STORE_F32>(p, stream); break;
-    case OV_EPI_ACCUM_F32 * 1000 + 128: LaunchTyped<128, OV_EPI_ACCUM_F32>(p, stream); break;
-    case OV_EPI_ACCUM_F32 * 1000 + 256: LaunchTyped<256, OV_EPI_ACCUM_F32>(p, stream); break;
-    case OV_EPI_SWIGLU_F16 * 1000 + 128: LaunchTyped<128, OV_EPI_SWIGLU_F16>(p, stream); break;
-    case OV_EPI_SWIGLU_F16 * 1000 + 256: LaunchTyped<256, OV_EPI_SWIGLU_F16>(p, stream); break;
-    case OV_EPI_QKNORM_ROPE_F16 * 1000 + 128:
-      LaunchTyped<128, OV_EPI_QKNORM_ROPE_F16>(p, stream);
-      break;
+#define OV_LAUNCH_CASE(BN, EPI)                                                 \
+  case EPI * 1000 + BN:                                                         \
+    SetMaxDynamicSmem(reinterpret_cast<const void*>(gemm_kernel<BN, EPI>),      \
+                      static_cast<int>(TileConfig<BN, EPI>::kSmemBytes));       \
+    LaunchTyped<BN, EPI>(p, stream);                                            \
+    break;
+    OV_GEMM_INSTANCES(OV_LAUNCH_CASE)
+#undef OV_LAUNCH_CASE
     default: throw Error(OV_ERR_UNSUPPORTED, "no GEMM kernel for this epilogue / tile");
   }
 }
@@ -484,13 +621,13 @@ void LaunchGemm(const GemmPlan& p, cudaStream_t stream) {
 
 // ------------------------------------------------ allocation-free variant
 //
-// ov_gemm_f16_noalloc takes its split-K scratch from this file-scope device
-// array instead of a caller-supplied workspace.  Every GPU that loads the
-// library holds it until the process exits.  In host code the array's name
-// only stands for the symbol, so its device address is looked up with
-// cudaGetSymbolAddress once per device (with that device current) and that
-// address is what the kernel receives.
-constexpr size_t kNoAllocScratchBytes = size_t{10} << 20;  // 10 MiB per device
+// ov_gemm_f16_noalloc takes its split-K scratch (the per-tile order
+// counters) from this file-scope device array instead of a caller-supplied
+// workspace.  Every GPU that loads the library holds it until the process
+// exits.  In host code the array's name only stands for the symbol, so its
+// device address is looked up with cudaGetSymbolAddress once per device
+// (with that device current) and that address is what the kernel receives.
+constexpr size_t kNoAllocScratchBytes = size_t{64} << 10;  // 64 KiB per device
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 // Bounded waits of this variant report into this word (it allocates nothing,
 // so it cannot use the lazily allocated device error word).
@@ -504,13 +641,6 @@ std::mutex g_noalloc_mutex;
 uint8_t* g_noalloc_scratch_ptr[kNoAllocDevices] = {};
 uint32_t* g_noalloc_status_ptr[kNoAllocDevices] = {};
 
-template <int BN, int EPI>
-void SetSmemDirect() {
-  Check(cudaFuncSetAttribute(gemm_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(TileConfig<BN>::kSmemBytes)),
-        "cudaFuncSetAttribute(max dynamic shared memory)");
-}
-
 // Once per device, with it current: device addresses of the static arrays,
 // cleared split-K counters, and the kernels' shared-memory limits.
 void NoAllocSetup(uint8_t** scratch, uint32_t** status) {
@@ -523,27 +653,19 @@ void NoAllocSetup(uint8_t** scratch, uint32_t** status) {
     void* tp = nullptr;
     Check(cudaGetSymbolAddress(&sp, g_noalloc_scratch), "cudaGetSymbolAddress(scratch)");
     Check(cudaGetSymbolAddress(&tp, g_noalloc_status), "cudaGetSymbolAddress(status)");
-    Check(cudaMemset(sp, 0, kCounterBytes), "clear split-K counters");
+    Check(cudaMemset(sp, 0, kNoAllocScratchBytes), "clear split-K counters");
     Check(cudaMemset(tp, 0, sizeof(uint32_t) * 64), "clear status word");
-    SetSmemDirect<128, OV_EPI_STORE_F32>();
-    SetSmemDirect<256, OV_EPI_STORE_F32>();
-    SetSmemDirect<128, OV_EPI_ACCUM_F32>();
-    SetSmemDirect<256, OV_EPI_ACCUM_F32>();
-    SetSmemDirect<128, OV_EPI_SWIGLU_F16>();
-    SetSmemDirect<256, OV_EPI_SWIGLU_F16>();
-    SetSmemDirect<128, OV_EPI_QKNORM_ROPE_F16>();
+#define OV_SET_DIRECT(BN, EPI)                                                                 \
+  Check(cudaFuncSetAttribute(gemm_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                             static_cast<int>(TileConfig<BN, EPI>::kSmemBytes)),               \
+        "cudaFuncSetAttribute(max dynamic shared memory)");
+    OV_GEMM_INSTANCES(OV_SET_DIRECT)
+#undef OV_SET_DIRECT
     g_noalloc_status_ptr[device] = static_cast<uint32_t*>(tp);
     g_noalloc_scratch_ptr[device] = static_cast<uint8_t*>(sp);
   }
   *scratch = g_noalloc_scratch_ptr[device];
   *status = g_noalloc_status_ptr[device];
-}
-
-template <int BN, int EPI>
-void LaunchDirect(const GemmPlan& p, cudaStream_t stream) {
-  gemm_kernel<BN, EPI><<<p.grid, kThreads, TileConfig<BN>::kSmemBytes, stream>>>(p.map_a, p.map_b,
-                                                                                p.args);
-  Check(cudaGetLastError(), "gemm kernel launch");
 }
 
 }  // namespace
@@ -611,20 +733,23 @@ int ov_gemm_f16_noalloc(const uint16_t* x, size_t ldx, const uint16_t* w, void* 
     PlanGemm(&plan, x, static_cast<int64_t>(ldx), w, static_cast<int64_t>(out), 0, y,
              static_cast<int64_t>(ldy), static_cast<int>(rows), static_cast<int>(out),
              static_cast<int>(in), epilogue, args, scratch, kNoAllocScratchBytes, sms, status);
-    const cudaStream_t s = AsStream(stream);
     switch (plan.epilogue * 1000 + plan.bn) {
-      case OV_EPI_STORE_F32 * 1000 + 128: LaunchDirect<128, OV_EPI_STORE_F32>(plan, s); break;
-      case OV_EPI_STORE_F32 * 1000 + 256: LaunchDirect<256, OV_EPI_STORE_F32>(plan, s); break;
-      case OV_EPI_ACCUM_F32 * 1000 + 128: LaunchDirect<128, OV_EPI_ACCUM_F32>(plan, s); break;
-      case OV_EPI_ACCUM_F32 * 1000 + 256: LaunchDirect<256, OV_EPI_ACCUM_F32>(plan, s); break;
-      case OV_EPI_SWIGLU_F16 * 1000 + 128: LaunchDirect<128, OV_EPI_SWIGLU_F16>(plan, s); break;
-      case OV_EPI_SWIGLU_F16 * 1000 + 256: LaunchDirect<256, OV_EPI_SWIGLU_F16>(plan, s); break;
-      case OV_EPI_QKNORM_ROPE_F16 * 1000 + 128:
-        LaunchDirect<128, OV_EPI_QKNORM_ROPE_F16>(plan, s);
-        break;
+#define OV_DIRECT_CASE(BN, EPI) \
+  case EPI * 1000 + BN: LaunchTyped<BN, EPI>(plan, AsStream(stream)); break;
+      OV_GEMM_INSTANCES(OV_DIRECT_CASE)
+#undef OV_DIRECT_CASE
       default: throw Error(OV_ERR_UNSUPPORTED, "no GEMM kernel for this epilogue / tile");
     }
   });
 }
 
 }  // extern "C"
+
+#ifdef OV_GEMM_TRACE
+extern "C" int ov_debug_gemm_trace(unsigned long long* out, size_t count) {
+  return cudaMemcpyFromSymbol(out, ovb::g_gemm_trace, count * sizeof(unsigned long long)) ==
+                 cudaSuccess
+             ? 0
+             : 2;
+}
+#endif

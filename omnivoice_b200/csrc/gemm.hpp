@@ -20,10 +20,13 @@ struct GemmArgs {
   int kblocks = 0;  // K / 64
   int splits = 1;   // split-K factor (OV_EPI_ACCUM_F32 only)
   int b_row_offset = 0;
-  int64_t ldy = 0;  // y row stride in elements of the output type
-  void* y = nullptr;
-  float* partials = nullptr;     // split-K partial tiles
-  uint32_t* counters = nullptr;  // split-K arrival counters, one per tile
+  int num_m = 0;    // 128-row tiles
+  int num_n = 0;    // BN-column tiles
+  int units = 0;    // num_m * num_n * splits work units
+  int out_cols = 0; // columns of y (N, or N / 2 for SwiGLU)
+  // Split-K order counters, one per tile: split s adds its partial into y
+  // after splits 0..s-1 did, so the sum order is fixed.
+  uint32_t* counters = nullptr;
   // OV_EPI_QKNORM_ROPE_F16
   const float* q_norm = nullptr;
   const float* k_norm = nullptr;
@@ -40,6 +43,7 @@ struct GemmArgs {
 struct GemmPlan {
   CUtensorMap map_a;
   CUtensorMap map_b;
+  CUtensorMap map_y;
   GemmArgs args;
   dim3 grid;
   int bn = 128;
@@ -53,15 +57,16 @@ struct GemmShapeChoice {
 };
 
 // Tile width and split-K factor for a product of this shape on `sms` SMs.
+// OV_GEMM_TILE=<bn>x<splits> in the environment overrides the choice
+// (tuning aid; ignored when the override is not valid for the product).
 GemmShapeChoice ChooseGemmShape(int M, int N, int K, int epilogue, bool have_workspace, int sms);
 // Workspace bytes a plan with this shape needs for split-K (0 if none).
 size_t GemmWorkspaceBytes(int M, int N, int K, int epilogue, int sms);
 
 // Builds a plan.  `w_rows` is the number of rows of the (possibly stacked)
 // weight tensor w points at and b_row_offset the first row this product
-// uses, so one tensor map can cover all layers.
-// `err` is the word bounded waits report into (nullptr: the device error
-// word of ov_take_device_errors).
+// uses, so one tensor map can cover all layers.  `err` is the word bounded
+// waits report into (nullptr: the device error word of ov_take_device_errors).
 void PlanGemm(GemmPlan* plan, const uint16_t* x, int64_t ldx, const uint16_t* w, int64_t w_rows,
               int b_row_offset, void* y, int64_t ldy, int M, int N, int K, int epilogue,
               const ov_epilogue_args* epilogue_args, void* workspace, size_t workspace_bytes,

@@ -9,10 +9,46 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <utility>
 
+#include "internal.hpp"
 #include "pack.hpp"
 
 namespace ovb {
+
+// Programmatic dependent launch (PDL) for the kernels of a generator step:
+// while a PdlScope(true) is alive on this thread, Launch() marks kernels so
+// the next one may start (prologue, weight prefetch) before the previous one
+// finishes; every kernel calls pdl_wait() before reading its inputs.
+bool PdlEnabled();
+class PdlScope {
+ public:
+  explicit PdlScope(bool on);
+  ~PdlScope();
+  PdlScope(const PdlScope&) = delete;
+  PdlScope& operator=(const PdlScope&) = delete;
+
+ private:
+  bool previous_;
+};
+
+template <typename... KernelArgs, typename... Args>
+void Launch(void (*kernel)(KernelArgs...), dim3 grid, dim3 block, size_t smem,
+            cudaStream_t stream, const char* what, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  if (PdlEnabled()) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  Check(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...), what);
+}
 
 void LaunchEmbed(const float* text_table, size_t text_vocab, const int32_t* row_text_ids,
                  const float* audio_table, size_t audio_vocab, const int32_t* ids,
@@ -25,9 +61,12 @@ void LaunchRmsNorm(const float* input, const int32_t* indices, size_t rows, cons
 
 void EncodeQkvMap(CUtensorMap* map, const uint16_t* qkv, int64_t ld_qkv, int64_t rows,
                   int64_t width);
+// items: device [n_items][2] (sequence, pair of 128-query tiles), longest
+// sequences first; null covers ceil(max_seqlen / 256) pairs of every
+// sequence (CTAs past a sequence's end exit at once).
 void LaunchAttention(const CUtensorMap& map_qkv, const int32_t* cu_seqlens, int num_seqs,
-                     int max_seqlen, int heads, int kv_heads, float scale, __half* out,
-                     int64_t ld_out, cudaStream_t stream);
+                     int max_seqlen, const int32_t* items, int n_items, int heads, int kv_heads,
+                     float scale, __half* out, int64_t ld_out, cudaStream_t stream);
 
 void LaunchScore(const float* logits, int64_t ld, int total_frames, int codebooks, int vocab,
                  uint32_t mask_id, float guidance, const UttDesc* utts, const int32_t* frame_utt,

@@ -88,6 +88,14 @@ void LaunchFillInt(int32_t* out, size_t count, int32_t value, cudaStream_t strea
   Check(cudaGetLastError(), "fill launch");
 }
 
+namespace {
+thread_local bool t_pdl = false;
+}  // namespace
+
+bool PdlEnabled() { return t_pdl; }
+PdlScope::PdlScope(bool on) : previous_(t_pdl) { t_pdl = on; }
+PdlScope::~PdlScope() { t_pdl = previous_; }
+
 void SetMaxDynamicSmem(const void* func, int bytes) {
   int device = 0;
   Check(cudaGetDevice(&device), "cudaGetDevice");

@@ -213,6 +213,34 @@ def test_gemm_residual_split_k_is_deterministic(M, K):
     assert torch.equal(outs[1], outs[2])  # split-K sums in a fixed order
 
 
+@pytest.mark.parametrize("tile", ["64x1", "128x1", "256x1", "64x3", "128x2", "256x4"])
+@pytest.mark.parametrize("epi", [N.OV_EPI_STORE_F32, N.OV_EPI_ACCUM_F32])
+def test_gemm_every_tile_shape(monkeypatch, tile, epi):
+    """Each compiled tile width (and split-K factor for the residual add),
+    forced through OV_GEMM_TILE, against float64 on ragged M and N."""
+    if epi == N.OV_EPI_STORE_F32 and not tile.endswith("x1"):
+        pytest.skip("split-K applies to the residual epilogue only")
+    monkeypatch.setenv("OV_GEMM_TILE", tile)
+    g = torch.Generator().manual_seed(7)
+    M, N_, K = 333, 1000, 1024
+    x = torch.randn(M, K, generator=g).half().cuda()
+    w = (torch.randn(N_, K, generator=g) * 0.02).half().cuda()
+    base = torch.randn(M, N_, generator=g).cuda()
+    ws = torch.zeros(4096, dtype=torch.uint8, device="cuda")
+    outs = []
+    for _ in range(2):
+        y = base.clone()
+        gemm(x, w, y, epi, workspace=ws)
+        outs.append(y)
+    torch.cuda.synchronize()
+    ref = x.double() @ w.double().T
+    if epi == N.OV_EPI_ACCUM_F32:
+        ref = ref + base.double()
+    bound = K * 2.0 ** -23 * (x.double().abs() @ w.double().abs().T) + 1e-5 * base.double().abs() + 1e-6
+    assert ((outs[0].double() - ref).abs() <= bound).all()
+    assert torch.equal(outs[0], outs[1])
+
+
 def test_gemm_swiglu_epilogue():
     g = torch.Generator().manual_seed(11)
     M, K, I = 333, 1024, 3072
@@ -272,17 +300,25 @@ def attention_reference(qkv, bounds, heads, kv_heads):
     return out.view(rows, heads * 128)
 
 
-@pytest.mark.parametrize("lengths", [[1], [5, 127], [128, 129], [370, 250], [140, 100, 705, 375],
-                                     [1425, 750]])
-def test_attention_varlen(lengths):
+@pytest.mark.parametrize("lengths,growing", [([1], False), ([5, 127], False), ([128, 129], False),
+                                             ([370, 250], False), ([140, 100, 705, 375], False),
+                                             ([1425, 750], False), ([700, 1300], True)])
+def test_attention_varlen(lengths, growing):
     g = torch.Generator().manual_seed(sum(lengths))
     heads, kv = 16, 8
     rows = sum(lengths)
     width = (heads + 2 * kv) * 128
-    qkv = (torch.randn(rows, width, generator=g) * 1.5).half()
+    qkv = torch.randn(rows, width, generator=g) * 1.5
     bounds = [0]
     for n in lengths:
         bounds.append(bounds[-1] + n)
+    if growing:
+        # Keys grow along each sequence: the running row maximum rises by
+        # many powers of two from one key tile to the next.
+        for s, e in zip(bounds[:-1], bounds[1:]):
+            ramp = torch.linspace(0.2, 6.0, e - s).unsqueeze(1)
+            qkv[s:e, heads * 128:(heads + kv) * 128] *= ramp
+    qkv = qkv.half()
     cu = torch.tensor(bounds, dtype=torch.int32).cuda()
     out = torch.full((rows, heads * 128), float("nan"), device="cuda", dtype=torch.float16)
     qkv_d = qkv.cuda()
