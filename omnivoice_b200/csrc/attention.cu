@@ -51,6 +51,48 @@ constexpr uint32_t kTile = 2 * kHalfTile;     // [128][128] half: 32 KB
 constexpr uint32_t kSmemBytes = 2 * kTile /*Q0,Q1*/ + 2 * 2 * kTile /*K,V ring*/ + 1024 + 256;
 constexpr float kRescaleThreshold = 8.0f;     // log2 units: P stays below 2^8
 
+// 2^x by the MUFU instruction (relative error far below the half rounding
+// the probabilities get); 2^-inf = +0.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Scores of keys at or past `valid` (outside the sequence) become -inf.
+__device__ __forceinline__ void mask_keys(uint32_t (&r)[32], int first, int valid) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j)
+    if (first + j >= valid) r[j] = 0xFF800000u;
+}
+
+__device__ __forceinline__ float max32(const uint32_t (&r)[32]) {
+  float v[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) v[j] = fmaxf(__uint_as_float(r[j]), __uint_as_float(r[j + 16]));
+#pragma unroll
+  for (int w = 8; w > 0; w >>= 1)
+#pragma unroll
+    for (int j = 0; j < w; ++j) v[j] = fmaxf(v[j], v[j + w]);
+  return v[0];
+}
+
+// p = 2^(s * scale - m) for 32 scores, packed as 16 half pairs; returns the
+// sum of the unrounded p.
+__device__ __forceinline__ float probs32(const uint32_t (&r)[32], float scale, float neg_m,
+                                         uint32_t (&packed)[16]) {
+  float a = 0.0f, b = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 32; j += 2) {
+    const float p0 = ex2_approx(fmaf(__uint_as_float(r[j]), scale, neg_m));
+    const float p1 = ex2_approx(fmaf(__uint_as_float(r[j + 1]), scale, neg_m));
+    a += p0;
+    b += p1;
+    packed[j / 2] = pack_half2(p0, p1);
+  }
+  return a + b;
+}
+
 struct AttnArgs {
   const int32_t* cu_seqlens;
   const int32_t* items;  // [n][2] (sequence, tile pair) or null: blockIdx.y/x
@@ -226,16 +268,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after_sync();
       const int valid = min(kKeys, len - t * kKeys);
-      // Pass 1: row maximum of the valid scores (registers hold one chunk).
+      // Pass 1: row maximum (two 32-column chunks in registers at a time;
+      // keys past the sequence end read as -inf).
       float mt = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(s_addr + c * 32, r);
+      for (int half = 0; half < 2; ++half) {
+        uint32_t ra[32], rb[32];
+        tmem_ld_32x32b_x32(s_addr + half * 64, ra);
+        tmem_ld_32x32b_x32(s_addr + half * 64 + 32, rb);
         tmem_ld_wait();
-#pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (c * 32 + j < valid) mt = fmaxf(mt, __uint_as_float(r[j]));
+        if (valid < kKeys) {
+          mask_keys(ra, half * 64, valid);
+          mask_keys(rb, half * 64 + 32, valid);
+        }
+        mt = fmaxf(mt, fmaxf(max32(ra), max32(rb)));
       }
       mt *= args.scale_log2;
       if (t == 0) {
@@ -249,7 +295,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // The previous P V of this group completed before S_t was written
           // (one thread issues both, in order), so O is stable here.
           const float m_new = grow ? mt : m;
-          const float alpha = exp2f(m - m_new);
+          const float alpha = ex2_approx(m - m_new);
           l *= alpha;
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
@@ -269,23 +315,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Pass 2: probabilities, written as half pairs over the consumed S
       // columns (keys 32c..32c+31 -> columns 16c..16c+15).
       float rowsum = 0.0f;
+      const float neg_m = -m;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(s_addr + c * 32, r);
+      for (int half = 0; half < 2; ++half) {
+        uint32_t ra[32], rb[32];
+        tmem_ld_32x32b_x32(s_addr + half * 64, ra);
+        tmem_ld_32x32b_x32(s_addr + half * 64 + 32, rb);
         tmem_ld_wait();
-        uint32_t packed[16];
-#pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          const int k = c * 32 + j;
-          const float p0 =
-              k < valid ? exp2f(fmaf(__uint_as_float(r[j]), args.scale_log2, -m)) : 0.0f;
-          const float p1 =
-              k + 1 < valid ? exp2f(fmaf(__uint_as_float(r[j + 1]), args.scale_log2, -m)) : 0.0f;
-          rowsum += p0 + p1;
-          packed[j / 2] = pack_half2(p0, p1);
+        if (valid < kKeys) {
+          mask_keys(ra, half * 64, valid);
+          mask_keys(rb, half * 64 + 32, valid);
         }
-        tmem_st_32x32b_x16(s_addr + c * 16, packed);
+        uint32_t pa[16], pb[16];
+        rowsum += probs32(ra, args.scale_log2, neg_m, pa);
+        rowsum += probs32(rb, args.scale_log2, neg_m, pb);
+        tmem_st_32x32b_x16(s_addr + half * 32, pa);
+        tmem_st_32x32b_x16(s_addr + half * 32 + 16, pb);
       }
       l += rowsum;
       tmem_st_wait();

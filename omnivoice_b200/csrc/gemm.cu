@@ -72,6 +72,17 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
   return __fdividef(g, 1.0f + __expf(-g)) * u;
 }
 
+// Shared-memory 16-byte load kept in program order with the tensor-memory
+// loads around it (a volatile asm): the compiler does not hoist a head's
+// worth of norm weights into registers ahead of use.
+__device__ __forceinline__ float4 lds_in_order(const float* p) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(smem_u32(p)));
+  return v;
+}
+
 // Unit u -> (m tile, n tile, split).  Tiles are visited in groups of
 // kGroupM m tiles, all n tiles of a group before the next group, so a
 // group's activations stay in L2 while the weights stream past.
@@ -95,6 +106,36 @@ struct EpilogueCtx {
   int ep;                // 0..127
   int row;               // tile row = tensor-memory lane
 };
+
+// RoPE cos / sin of one row's position (QK-norm epilogue), loaded before
+// the accumulator is ready so the loads overlap the tile's MMAs.
+struct RopeRow {
+  float4 c[16];
+  float4 s[16];
+};
+
+template <int EPI>
+__device__ __forceinline__ void LoadRopeRow(const GemmArgs& a, int m_tile, int row, RopeRow& r) {
+  if constexpr (EPI == OV_EPI_QKNORM_ROPE_F16) {
+    const int64_t grow = static_cast<int64_t>(m_tile) * kBM + row;
+    int pos = grow < a.M ? __ldg(a.positions + grow) : 0;
+    if (pos < 0 || pos >= a.max_positions) {
+      atomicOr(a.err, kErrBadArgument);
+      pos = 0;
+    }
+    const float4* cs = reinterpret_cast<const float4*>(a.rope_cos + static_cast<int64_t>(pos) * 64);
+    const float4* sn = reinterpret_cast<const float4*>(a.rope_sin + static_cast<int64_t>(pos) * 64);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      r.c[k] = __ldg(cs + k);
+      r.s[k] = __ldg(sn + k);
+    }
+  }
+}
+
+__device__ __forceinline__ float F4At(const float4& v, int i) {
+  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
 
 // Writes this thread's 128-byte row piece into the next staging tile and
 // has one thread store (or reduce-add) the tile at column x, row y0.
@@ -124,7 +165,8 @@ __device__ __forceinline__ void EmitChunk(EpilogueCtx& c, const CUtensorMap* map
 template <int BN, int EPI>
 __device__ __forceinline__ void EpilogueUnit(const GemmArgs& a, const CUtensorMap* map_y,
                                              EpilogueCtx& c, uint32_t tacc, int m_tile,
-                                             int n_tile, const float* norm_w) {
+                                             int n_tile, const float* norm_w,
+                                             const RopeRow& rope) {
   const int y0 = m_tile * kBM;
   if constexpr (EPI == OV_EPI_STORE_F32 || EPI == OV_EPI_ACCUM_F32) {
 #pragma unroll 1
@@ -158,61 +200,168 @@ __device__ __forceinline__ void EpilogueUnit(const GemmArgs& a, const CUtensorMa
       EmitChunk<false>(c, map_y, out, n_tile * (BN / 2) + gi * G, y0);
     }
   } else if constexpr (EPI == OV_EPI_QKNORM_ROPE_F16) {
-    static_assert(BN == 128, "one head of 128 per tile");
-    float v[128];
+    // BN / 128 heads per tile.  Tensor memory is read in 16-column pieces,
+    // several times over (RMS first, then the low and the high half of the
+    // rotated pairs (i, i + 64)), so a thread never holds more than one
+    // output row piece besides its RoPE row.
+    static_assert(BN % 128 == 0, "whole heads per tile");
+#pragma unroll 1
+    for (int hh = 0; hh < BN / 128; ++hh) {
+      const int slot = n_tile * (BN / 128) + hh;
+      const uint32_t th = tacc + hh * 128;
+      if (slot < a.heads + a.kv_heads) {
+        const float* w = norm_w + (slot < a.heads ? 0 : 128);
+        float ss = 0.0f;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      uint32_t r[32];
-      tmem_ld_32x32b_x32(tacc + q * 32, r);
-      tmem_ld_wait();
+        for (int q = 0; q < 8; ++q) {
+          uint32_t r[16];
+          tmem_ld_32x32b_x16(th + q * 16, r);
+          tmem_ld_wait();
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[q * 32 + j] = __uint_as_float(r[j]);
-    }
-    const int slot = n_tile;
-    uint32_t lo[32], hi[32];
-    if (slot < a.heads + a.kv_heads) {
-      const float* w = norm_w + (slot < a.heads ? 0 : 128);
-      float ss = 0.0f;
-#pragma unroll
-      for (int j = 0; j < 128; ++j) ss = fmaf(v[j], v[j], ss);
-      const float scale = 1.0f / sqrtf(ss / 128.0f + a.epsilon);
-      const int64_t grow = static_cast<int64_t>(y0) + c.row;
-      int pos = grow < a.M ? a.positions[grow] : 0;
-      if (pos < 0 || pos >= a.max_positions) {
-        atomicOr(a.err, kErrBadArgument);
-        pos = 0;
-      }
-      const float4* cs = reinterpret_cast<const float4*>(a.rope_cos + static_cast<int64_t>(pos) * 64);
-      const float4* sn = reinterpret_cast<const float4*>(a.rope_sin + static_cast<int64_t>(pos) * 64);
-#pragma unroll
-      for (int i4 = 0; i4 < 16; ++i4) {
-        const float4 c4 = __ldg(cs + i4);
-        const float4 s4 = __ldg(sn + i4);
-        const float cc[4] = {c4.x, c4.y, c4.z, c4.w};
-        const float ssn[4] = {s4.x, s4.y, s4.z, s4.w};
-        float l4[4], h4[4];
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const int i = i4 * 4 + t;
-          const float x1 = w[i] * (v[i] * scale);
-          const float x2 = w[i + 64] * (v[i + 64] * scale);
-          l4[t] = __fsub_rn(__fmul_rn(x1, cc[t]), __fmul_rn(x2, ssn[t]));
-          h4[t] = __fadd_rn(__fmul_rn(x2, cc[t]), __fmul_rn(x1, ssn[t]));
+          for (int j = 0; j < 16; ++j) ss = fmaf(__uint_as_float(r[j]), __uint_as_float(r[j]), ss);
         }
-        lo[i4 * 2] = pack_half2(l4[0], l4[1]);
-        lo[i4 * 2 + 1] = pack_half2(l4[2], l4[3]);
-        hi[i4 * 2] = pack_half2(h4[0], h4[1]);
-        hi[i4 * 2 + 1] = pack_half2(h4[2], h4[3]);
-      }
-    } else {
+        const float scale = 1.0f / sqrtf(ss / 128.0f + a.epsilon);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        lo[j] = pack_half2(v[2 * j], v[2 * j + 1]);
-        hi[j] = pack_half2(v[64 + 2 * j], v[64 + 2 * j + 1]);
+        for (int part = 0; part < 2; ++part) {  // 0: columns 0..63, 1: 64..127
+          uint32_t out[32];
+#pragma unroll
+          for (int i0 = 0; i0 < 64; i0 += 16) {
+            uint32_t r1[16], r2[16];
+            tmem_ld_32x32b_x16(th + i0, r1);
+            tmem_ld_32x32b_x16(th + 64 + i0, r2);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i4 = 0; i4 < 4; ++i4) {
+              const float4 w14 = lds_in_order(w + i0 + i4 * 4);
+              const float4 w24 = lds_in_order(w + 64 + i0 + i4 * 4);
+              float o4[4];
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                const int i = i0 + i4 * 4 + t;
+                const float cc = F4At(rope.c[i / 4], t);
+                const float sn = F4At(rope.s[i / 4], t);
+                const float x1 = F4At(w14, t) * (__uint_as_float(r1[i4 * 4 + t]) * scale);
+                const float x2 = F4At(w24, t) * (__uint_as_float(r2[i4 * 4 + t]) * scale);
+                o4[t] = part == 0 ? __fsub_rn(__fmul_rn(x1, cc), __fmul_rn(x2, sn))
+                                  : __fadd_rn(__fmul_rn(x2, cc), __fmul_rn(x1, sn));
+              }
+              out[i0 / 2 + i4 * 2] = pack_half2(o4[0], o4[1]);
+              out[i0 / 2 + i4 * 2 + 1] = pack_half2(o4[2], o4[3]);
+            }
+          }
+          EmitChunk<false>(c, map_y, out, slot * 128 + part * 64, y0);
+        }
+      } else {
+        // v heads: plain half conversion.
+#pragma unroll
+        for (int part = 0; part < 2; ++part) {
+          uint32_t out[32];
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(th + part * 64 + q * 32, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              out[q * 16 + j] = pack_half2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+          }
+          EmitChunk<false>(c, map_y, out, slot * 128 + part * 64, y0);
+        }
       }
     }
-    EmitChunk<false>(c, map_y, lo, slot * 128, y0);
-    EmitChunk<false>(c, map_y, hi, slot * 128 + 64, y0);
+  }
+}
+
+// Cluster split-K.  After every CTA of the cluster has finished its MMAs
+// (a cluster barrier), the idle operand ring of each CTA holds an inbox of
+// S - 1 slots followed by an outbox of S - 1 slots, each [128 rows][BN / S]
+// floats with 16-byte pieces XOR-swizzled by row.  Rank r owns column slice
+// r of the tile.
+
+// Slot of rank `other` among the S - 1 ranks other than `self`.
+__device__ __forceinline__ int PeerSlot(int other, int self) { return other < self ? other : other - 1; }
+
+// Step 1 (epilogue thread `row`): every other rank's slice of this CTA's
+// partial goes from tensor memory into the outbox; then one thread sends
+// each outbox slot to its rank's inbox with a bulk copy that completes on
+// that rank's inbox barrier.
+template <int BN>
+__device__ __forceinline__ void ClusterSend(uint32_t tacc, uint8_t* ring, const EpilogueCtx& c,
+                                            int rank, int splits, uint64_t* inbox_bar) {
+  const int cols = BN / splits;
+  const uint32_t slot_bytes = static_cast<uint32_t>(kBM * cols * 4);
+  uint8_t* outbox = ring + (splits - 1) * slot_bytes;
+#pragma unroll 1
+  for (int j = 0; j < splits; ++j) {
+    if (j == rank) continue;
+    uint8_t* slot = outbox + PeerSlot(j, rank) * slot_bytes;
+#pragma unroll 1
+    for (int cc = 0; cc < cols; cc += 32) {
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(tacc + static_cast<uint32_t>(j * cols + cc), v);
+      tmem_ld_wait();
+      uint8_t* dst = slot + (c.row * cols + cc) * 4;
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        *reinterpret_cast<uint4*>(dst + ((q ^ (c.row & 7)) << 4)) =
+            make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    }
+  }
+  fence_proxy_async_smem();
+  named_barrier(1, 128);
+  if (c.ep == 0) {
+    const uint32_t inbox = smem_u32(ring);
+    for (int j = 0; j < splits; ++j) {
+      if (j == rank) continue;
+      const uint32_t src = smem_u32(outbox + PeerSlot(j, rank) * slot_bytes);
+      const uint32_t dst = mapa_shared(inbox + PeerSlot(rank, j) * slot_bytes, j);
+      bulk_copy_to_peer(dst, src, slot_bytes, mapa_shared(smem_u32(inbox_bar), j));
+    }
+  }
+}
+
+// Step 2: this rank's slice is the sum of the splits' partials in split
+// order (its own from tensor memory, the others from the inbox), stored or
+// added into y like an unsplit tile.
+template <int BN, int EPI>
+__device__ __forceinline__ void ClusterReduce(const GemmArgs& a, const CUtensorMap* map_y,
+                                              EpilogueCtx& c, uint32_t tacc, const uint8_t* ring,
+                                              int m_tile, int n_tile, int rank) {
+  const int splits = a.splits;
+  const int cols = BN / splits;
+  const int slot_bytes = kBM * cols * 4;
+  const int y0 = m_tile * kBM;
+#pragma unroll 1
+  for (int cc = 0; cc < cols; cc += 32) {
+    const int x = n_tile * BN + rank * cols + cc;
+    if (x >= a.out_cols) break;  // uniform over the epilogue threads
+    float acc[32];
+#pragma unroll
+    for (int e = 0; e < 32; ++e) acc[e] = 0.0f;
+#pragma unroll 1
+    for (int j = 0; j < splits; ++j) {
+      if (j == rank) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tacc + static_cast<uint32_t>(rank * cols + cc), v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) acc[e] += __uint_as_float(v[e]);
+      } else {
+        const uint8_t* src = ring + PeerSlot(j, rank) * slot_bytes + (c.row * cols + cc) * 4;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 t = *reinterpret_cast<const float4*>(src + ((q ^ (c.row & 7)) << 4));
+          acc[4 * q] += t.x;
+          acc[4 * q + 1] += t.y;
+          acc[4 * q + 2] += t.z;
+          acc[4 * q + 3] += t.w;
+        }
+      }
+    }
+    uint32_t w[32];
+#pragma unroll
+    for (int e = 0; e < 32; ++e) w[e] = __float_as_uint(acc[e]);
+    EmitChunk<EPI == OV_EPI_ACCUM_F32>(c, map_y, w, x, y0);
   }
 }
 
@@ -233,6 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const __grid_constant__ CUtensorMap map_y, const GemmArgs args) {
   using Cfg = TileConfig<BN, EPI>;
   constexpr int kStages = Cfg::kStages;
+  constexpr bool kClusterSplit = EPI == OV_EPI_ACCUM_F32 || EPI == OV_EPI_STORE_F32;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -245,7 +395,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;  // [2]
   uint64_t* tempty = tfull + 2;       // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* inbox_bar = tempty + 2;   // cluster split-K: partials received
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(inbox_bar + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -260,6 +411,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 128);
     }
+    mbar_init(inbox_bar, 1);
     fence_mbar_init();
     tma_prefetch_map(&map_a);
     tma_prefetch_map(&map_b);
@@ -337,6 +489,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (uint32_t i = first; i < k_iter; ++i)
         (void)mbar_wait(&full[i % kStages], (i / kStages) & 1u, args.err);
     }
+    if (kClusterSplit && args.cluster) {  // the two barriers of the split-K reduction
+      __syncwarp();
+      cluster_sync();
+      cluster_sync();
+    }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_f16_f32(kBM, BN);
@@ -379,6 +536,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       OV_TRACE(11);
     }
+    if (kClusterSplit && args.cluster) {
+      __syncwarp();
+      cluster_sync();
+      cluster_sync();
+    }
   } else {
     EpilogueCtx c;
     c.staging = staging;
@@ -391,12 +553,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       int m_tile, n_tile, split;
       UnitCoords(args, u, m_tile, n_tile, split);
       const int buf = acc_iter & 1;
+      RopeRow rope;
+      LoadRopeRow<EPI>(args, m_tile, c.row, rope);
       // Every epilogue thread runs the epilogue even after a timed-out wait
       // (the error word is set) so the 128 threads stay in step.
       (void)mbar_wait(&tfull[buf], static_cast<uint32_t>(acc_iter >> 1) & 1u, args.err);
       __syncwarp();  // the tensor-memory loads below are warp-collective
       if (acc_iter == 0 && c.ep == 0) OV_TRACE(5);
       tc_fence_after_sync();
+      if (args.cluster) break;  // one unit per CTA, reduced below
       const int tile = u / args.splits;
       if (EPI == OV_EPI_ACCUM_F32 && args.splits > 1 && c.ep == 0) {
         // Earlier splits of this tile first; their adds are complete.
@@ -406,7 +571,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const uint32_t tacc =
           tmem + static_cast<uint32_t>(buf * BN) + (static_cast<uint32_t>(quarter * 32) << 16);
-      EpilogueUnit<BN, EPI>(args, &map_y, c, tacc, m_tile, n_tile, norm_w);
+      EpilogueUnit<BN, EPI>(args, &map_y, c, tacc, m_tile, n_tile, norm_w, rope);
       tc_fence_before_sync();
       mbar_arrive(&tempty[buf]);
       if (EPI == OV_EPI_ACCUM_F32 && args.splits > 1 && c.ep == 0) {
@@ -419,6 +584,30 @@ __global__ void __launch_bounds__(kThreads, 1)
           red_release_gpu_add(args.counters + tile, 1u);
       }
       if (acc_iter == 0 && c.ep == 0) OV_TRACE(6);
+    }
+    if constexpr (kClusterSplit) {
+      if (args.cluster) {
+        // Every CTA of the cluster has waited for its accumulator, so all
+        // MMAs are complete and every operand ring is free.
+        int m_tile, n_tile, split;
+        UnitCoords(args, blockIdx.x, m_tile, n_tile, split);
+        const uint32_t tacc = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+        __syncwarp();
+        tc_fence_before_sync();
+        cluster_sync();
+        tc_fence_after_sync();
+        if (c.ep == 0) {
+          const uint32_t slot_bytes = static_cast<uint32_t>(kBM * (BN / args.splits) * 4);
+          mbar_arrive_expect_tx(inbox_bar, static_cast<uint32_t>(args.splits - 1) * slot_bytes);
+        }
+        ClusterSend<BN>(tacc, smem, c, split, args.splits, inbox_bar);
+        (void)mbar_wait(inbox_bar, 0, args.err);
+        __syncwarp();
+        ClusterReduce<BN, EPI>(args, &map_y, c, tacc, smem, m_tile, n_tile, split);
+        // No CTA leaves while a peer's bulk copy may still read its outbox.
+        __syncwarp();
+        cluster_sync();
+      }
     }
     if (c.ep == 0) bulk_wait_group<0>();
 #ifdef OV_GEMM_TRACE
@@ -450,24 +639,48 @@ __global__ void __launch_bounds__(kThreads, 1)
   X(256, OV_EPI_ACCUM_F32)             \
   X(128, OV_EPI_SWIGLU_F16)            \
   X(256, OV_EPI_SWIGLU_F16)            \
-  X(128, OV_EPI_QKNORM_ROPE_F16)
+  X(128, OV_EPI_QKNORM_ROPE_F16)       \
+  X(256, OV_EPI_QKNORM_ROPE_F16)
 
 template <int BN, int EPI>
 void LaunchTyped(const GemmPlan& p, cudaStream_t stream) {
-  Launch(gemm_kernel<BN, EPI>, p.grid, dim3(kThreads), TileConfig<BN, EPI>::kSmemBytes, stream,
-         "gemm kernel launch", p.map_a, p.map_b, p.map_y, p.args);
+  LaunchEx(gemm_kernel<BN, EPI>, p.grid, dim3(kThreads), TileConfig<BN, EPI>::kSmemBytes, stream,
+           "gemm kernel launch", p.cluster_x, p.map_a, p.map_b, p.map_y, p.args);
 }
 
 int Tiles(int M, int N, int bn) { return ((M + kBM - 1) / kBM) * ((N + bn - 1) / bn); }
 
-bool ValidShape(int bn, int splits, int N, int K, int epilogue) {
+bool ValidShape(int bn, int splits, bool cluster, int N, int K, int epilogue) {
   if (splits < 1 || splits > 8) return false;
+  if (cluster) {
+    // Split-K inside a thread-block cluster: the splits' partials meet in
+    // distributed shared memory, each rank reducing a BN / splits slice.
+    if (splits != 2 && splits != 4 && splits != 8) return false;
+    if (epilogue != OV_EPI_ACCUM_F32 && epilogue != OV_EPI_STORE_F32) return false;
+    if (bn / splits < 32 || (K / kBK) < splits) return false;
+    // Inbox and outbox, (S - 1) slices each, live in the 192 KB operand ring.
+    if (2 * (splits - 1) * kBM * (bn / splits) * 4 > kRingBytes) return false;
+    return bn == 64 || bn == 128 || bn == 256;
+  }
   if (splits > 1 && (epilogue != OV_EPI_ACCUM_F32 || (K / kBK) / splits < 2)) return false;
   switch (epilogue) {
-    case OV_EPI_QKNORM_ROPE_F16: return bn == 128;
+    case OV_EPI_QKNORM_ROPE_F16: return (bn == 128 || bn == 256) && N % bn == 0;
     case OV_EPI_SWIGLU_F16: return (bn == 128 || bn == 256) && N % bn == 0;
     default: return bn == 64 || bn == 128 || bn == 256;
   }
+}
+
+// CTAs of one GEMM kernel that can be resident at once in clusters of
+// 1, 2, 4 and 8 (index log2), measured per device by ConfigureGemmKernels;
+// 0 until then (the chooser then assumes one cluster per 8 SMs).
+int g_cluster_ctas[64][4];
+
+int ClusterCapacity(int splits, int sms) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  const int idx = splits == 2 ? 1 : splits == 4 ? 2 : splits == 8 ? 3 : 0;
+  const int v = g_cluster_ctas[dev][idx];
+  return v > 0 ? v : (sms / 8) * 8;
 }
 
 }  // namespace
@@ -475,28 +688,43 @@ bool ValidShape(int bn, int splits, int N, int K, int epilogue) {
 GemmShapeChoice ChooseGemmShape(int M, int N, int K, int epilogue, bool have_workspace, int sms) {
   if (const char* env = std::getenv("OV_GEMM_TILE")) {
     int bn = 0, splits = 1;
-    if (std::sscanf(env, "%dx%d", &bn, &splits) >= 1 &&
-        ValidShape(bn, splits, N, K, epilogue) && (splits == 1 || have_workspace))
-      return {bn, splits};
+    char sep = 'x';
+    if (std::sscanf(env, "%d%c%d", &bn, &sep, &splits) >= 1) {
+      const bool cluster = sep == 'c';
+      if (ValidShape(bn, splits, cluster, N, K, epilogue) &&
+          (splits == 1 || cluster || have_workspace))
+        return {bn, splits, cluster && splits > 1};
+    }
   }
-  // Cost in units of (one 64-wide k block of a 128 x 64 tile): a unit of
-  // width bn over kb k blocks costs kb * bn / 64 * eff(bn) + fill, a
-  // persistent CTA runs ceil(units / sms) units one after another, and
-  // each extra split waits for the previous split's add (~ one chunk).
+  // Cost in units of one 64-deep k block of one CTA (about 0.3 us on
+  // B200, measured: the four tcgen05.mma of a k block take nearly the same
+  // time for BN = 64, 128 and 256).  A persistent CTA runs
+  // ceil(units / CTAs) units back to back; each kernel pays a fill
+  // (prologue, first loads, last epilogue, about 5 us); serialised split-K
+  // adds one tile reduction per extra split; cluster split-K one exchange
+  // of (S - 1) slices through distributed shared memory.
   const int kblocks = K / kBK;
-  auto eff = [](int bn) { return bn == 64 ? 1.35 : bn == 128 ? 1.08 : 1.0; };
-  GemmShapeChoice best{128, 1};
+  auto per_kblock = [](int bn) { return bn == 256 ? 1.03 : 1.0; };
+  constexpr double kFill = 17.0;
+  GemmShapeChoice best{128, 1, false};
   double best_cost = 1e300;
   for (int bn : {64, 128, 256}) {
-    for (int s = 1; s <= 4; ++s) {
-      if (!ValidShape(bn, s, N, K, epilogue) || (s > 1 && !have_workspace)) continue;
-      const double units = static_cast<double>(Tiles(M, N, bn)) * s;
-      const double rounds = std::ceil(units / sms);
-      const double per_unit = (static_cast<double>(kblocks) / s) * (bn / 64.0) * eff(bn) + 4.0;
-      const double cost = rounds * per_unit + (s - 1) * 3.0;
-      if (cost < best_cost - 1e-9) {
-        best_cost = cost;
-        best = {bn, s};
+    for (int s = 1; s <= 8; s *= 2) {
+      for (int cl = 0; cl < 2; ++cl) {
+        const bool cluster = cl == 1;
+        if (cluster && s == 1) continue;
+        if (!ValidShape(bn, s, cluster, N, K, epilogue)) continue;
+        if (s > 1 && !cluster && (!have_workspace || s > 4)) continue;
+        const double units = static_cast<double>(Tiles(M, N, bn)) * s;
+        const double ctas = cluster ? ClusterCapacity(s, sms) : sms;
+        const double rounds = std::ceil(units / ctas);
+        double cost = rounds * (static_cast<double>(kblocks) / s) * per_kblock(bn) + kFill;
+        if (s > 1)
+          cost += cluster ? 4.0 + (s - 1) * (kBM * (bn / s) * 4.0) / 8192.0 : (s - 1) * 12.0;
+        if (cost < best_cost - 1e-9) {
+          best_cost = cost;
+          best = {bn, s, cluster};
+        }
       }
     }
   }
@@ -505,7 +733,7 @@ GemmShapeChoice ChooseGemmShape(int M, int N, int K, int epilogue, bool have_wor
 
 size_t GemmWorkspaceBytes(int M, int N, int K, int epilogue, int sms) {
   const GemmShapeChoice c = ChooseGemmShape(M, N, K, epilogue, true, sms);
-  if (c.splits <= 1) return 0;
+  if (c.splits <= 1 || c.cluster) return 0;
   return static_cast<size_t>(Tiles(M, N, c.bn)) * sizeof(uint32_t);
 }
 
@@ -522,7 +750,7 @@ void PlanGemm(GemmPlan* plan, const uint16_t* x, int64_t ldx, const uint16_t* w,
   OV_REQUIRE((reinterpret_cast<uintptr_t>(y) & 15u) == 0, "y must be 16-byte aligned");
   GemmShapeChoice choice =
       ChooseGemmShape(M, N, K, epilogue, workspace != nullptr && workspace_bytes > 0, sms);
-  if (choice.splits > 1 &&
+  if (choice.splits > 1 && !choice.cluster &&
       workspace_bytes < static_cast<size_t>(Tiles(M, N, choice.bn)) * sizeof(uint32_t))
     choice = ChooseGemmShape(M, N, K, epilogue, false, sms);
   int out_cols = N;
@@ -554,7 +782,9 @@ void PlanGemm(GemmPlan* plan, const uint16_t* x, int64_t ldx, const uint16_t* w,
   a.units = a.num_m * a.num_n * a.splits;
   a.out_cols = out_cols;
   a.err = err != nullptr ? err : DeviceErrorWord();
-  if (choice.splits > 1) a.counters = static_cast<uint32_t*>(workspace);
+  if (choice.splits > 1 && !choice.cluster) a.counters = static_cast<uint32_t*>(workspace);
+  a.cluster = choice.cluster ? 1 : 0;
+  plan->cluster_x = choice.cluster ? static_cast<unsigned>(choice.splits) : 1u;
   if (ea != nullptr) {
     a.q_norm = ea->q_norm;
     a.k_norm = ea->k_norm;
@@ -583,8 +813,10 @@ void PlanGemm(GemmPlan* plan, const uint16_t* x, int64_t ldx, const uint16_t* w,
                       static_cast<uint64_t>(ldy) * 4, 32, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
   // With split-K every round of the persistent grid holds whole tiles, so a
   // split only waits for lower-numbered CTAs of its own round.
+  // Cluster split-K: one unit per CTA, the splits of a tile in one cluster.
   int grid = std::min(a.units, sms);
   if (a.splits > 1) grid = std::max(a.splits, grid / a.splits * a.splits);
+  if (a.cluster) grid = a.units;
   plan->grid = dim3(static_cast<unsigned>(grid), 1, 1);
   switch (epilogue * 1000 + choice.bn) {
 #define OV_SMEM_CASE(BN, EPI) \
@@ -601,6 +833,31 @@ void ConfigureGemmKernels() {
                     static_cast<int>(TileConfig<BN, EPI>::kSmemBytes));
   OV_GEMM_INSTANCES(OV_CONFIGURE)
 #undef OV_CONFIGURE
+  int dev = 0;
+  Check(cudaGetDevice(&dev), "get device");
+  if (dev < 0 || dev >= 64 || g_cluster_ctas[dev][0] > 0) return;
+  // Resident CTAs in clusters of 1..8 (every instance holds one CTA per SM).
+  for (int i = 0; i < 4; ++i) {
+    const unsigned size = 1u << i;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(size * 16, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = TileConfig<256, OV_EPI_ACCUM_F32>::kSmemBytes;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = size;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, gemm_kernel<256, OV_EPI_ACCUM_F32>, &cfg) !=
+        cudaSuccess) {
+      ClearError();
+      clusters = 0;
+    }
+    g_cluster_ctas[dev][i] = std::max(1, clusters * static_cast<int>(size));
+  }
 }
 
 void LaunchGemm(const GemmPlan& p, cudaStream_t stream) {

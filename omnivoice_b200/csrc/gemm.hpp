@@ -27,6 +27,10 @@ struct GemmArgs {
   // Split-K order counters, one per tile: split s adds its partial into y
   // after splits 0..s-1 did, so the sum order is fixed.
   uint32_t* counters = nullptr;
+  // 1: the splits of a tile run as one thread-block cluster (one unit per
+  // CTA, split = rank in the cluster) and add their partials in split order
+  // through distributed shared memory; no counters.
+  int cluster = 0;
   // OV_EPI_QKNORM_ROPE_F16
   const float* q_norm = nullptr;
   const float* k_norm = nullptr;
@@ -49,11 +53,13 @@ struct GemmPlan {
   int bn = 128;
   int epilogue = OV_EPI_STORE_F32;
   size_t smem_bytes = 0;
+  unsigned cluster_x = 1;  // CTAs per thread-block cluster
 };
 
 struct GemmShapeChoice {
   int bn;
   int splits;
+  bool cluster = false;  // splits reduced inside a thread-block cluster
 };
 
 // Tile width and split-K factor for a product of this shape on `sms` SMs.

@@ -32,22 +32,38 @@ class PdlScope {
   bool previous_;
 };
 
+// cluster_x > 1 launches thread-block clusters of cluster_x CTAs along x.
 template <typename... KernelArgs, typename... Args>
-void Launch(void (*kernel)(KernelArgs...), dim3 grid, dim3 block, size_t smem,
-            cudaStream_t stream, const char* what, Args&&... args) {
+void LaunchEx(void (*kernel)(KernelArgs...), dim3 grid, dim3 block, size_t smem,
+              cudaStream_t stream, const char* what, unsigned cluster_x, Args&&... args) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
   if (PdlEnabled()) {
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
   }
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = n > 0 ? attr : nullptr;
+  cfg.numAttrs = n;
   Check(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...), what);
+}
+
+template <typename... KernelArgs, typename... Args>
+void Launch(void (*kernel)(KernelArgs...), dim3 grid, dim3 block, size_t smem,
+            cudaStream_t stream, const char* what, Args&&... args) {
+  LaunchEx(kernel, grid, block, smem, stream, what, 1u, std::forward<Args>(args)...);
 }
 
 void LaunchEmbed(const float* text_table, size_t text_vocab, const int32_t* row_text_ids,

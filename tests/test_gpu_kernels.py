@@ -213,13 +213,15 @@ def test_gemm_residual_split_k_is_deterministic(M, K):
     assert torch.equal(outs[1], outs[2])  # split-K sums in a fixed order
 
 
-@pytest.mark.parametrize("tile", ["64x1", "128x1", "256x1", "64x3", "128x2", "256x4"])
+@pytest.mark.parametrize("tile", ["64x1", "128x1", "256x1", "64x3", "128x2", "256x4",
+                                  "64c2", "128c4", "256c2", "256c8"])
 @pytest.mark.parametrize("epi", [N.OV_EPI_STORE_F32, N.OV_EPI_ACCUM_F32])
 def test_gemm_every_tile_shape(monkeypatch, tile, epi):
-    """Each compiled tile width (and split-K factor for the residual add),
-    forced through OV_GEMM_TILE, against float64 on ragged M and N."""
-    if epi == N.OV_EPI_STORE_F32 and not tile.endswith("x1"):
-        pytest.skip("split-K applies to the residual epilogue only")
+    """Each compiled tile width, serialised split-K factor (<bn>x<splits>,
+    residual add only) and cluster split-K factor (<bn>c<splits>), forced
+    through OV_GEMM_TILE, against float64 on ragged M and N."""
+    if epi == N.OV_EPI_STORE_F32 and "x" in tile and not tile.endswith("x1"):
+        pytest.skip("serialised split-K applies to the residual epilogue only")
     monkeypatch.setenv("OV_GEMM_TILE", tile)
     g = torch.Generator().manual_seed(7)
     M, N_, K = 333, 1000, 1024
@@ -260,7 +262,9 @@ def test_gemm_swiglu_epilogue():
     assert (np.abs(got - ref) <= half_ulp(ref) + 1e-4).all()
 
 
-def test_gemm_qknorm_rope_epilogue_matches_standalone_math():
+@pytest.mark.parametrize("tile", ["128x1", "256x1"])
+def test_gemm_qknorm_rope_epilogue_matches_standalone_math(monkeypatch, tile):
+    monkeypatch.setenv("OV_GEMM_TILE", tile)
     g = torch.Generator().manual_seed(12)
     M, K, heads, kv = 300, 1024, 16, 8
     width = (heads + 2 * kv) * 128
