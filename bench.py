@@ -73,21 +73,16 @@ def batched_set(seed=4, count=64):
 
 
 def utterance_cost(text, ref, target):
-    L = text + ref + target
-    R = L + target
-    return 32 * (R * 880.80e6 + 229376.0 * (L * L + target * target) + 2 * target * 16.79e6)
+    from omnivoice_b200.scheduler import utterance_cost as cost
+    return cost(text + ref + target, target)
 
 
 def lpt_partition(specs, ranks):
-    """Longest-processing-time-first assignment of utterances to ranks."""
-    order = sorted(range(len(specs)), key=lambda i: -utterance_cost(*specs[i]))
-    load = [0.0] * ranks
-    parts = [[] for _ in range(ranks)]
-    for i in order:
-        r = min(range(ranks), key=lambda k: load[k])
-        parts[r].append(i)
-        load[r] += utterance_cost(*specs[i])
-    return parts, load
+    """Longest-processing-time-first assignment of utterances to ranks
+    (omnivoice_b200.scheduler, the same partition generate_data_parallel
+    uses)."""
+    from omnivoice_b200.scheduler import lpt_partition as lpt
+    return lpt([utterance_cost(*s) for s in specs], ranks)
 
 
 def make_workload(name, rank, world):
@@ -98,8 +93,10 @@ def make_workload(name, rank, world):
         mine = parts[rank]
         desc = "config4: 64 utterances, F~U[50,750], LPT-partitioned across ranks"
         total_audio = sum(s[2] for s in specs) / FRAME_RATE
-        return (desc, [inputs_all[i] for i in mine], [1000 + i for i in mine], total_audio,
-                "strong", {"imbalance_max_over_mean": max(load) / (sum(load) / world)})
+        seeds_all = [1000 + i for i in range(len(specs))]
+        return (desc, [inputs_all[i] for i in mine], [seeds_all[i] for i in mine], total_audio,
+                "strong", {"imbalance_max_over_mean": max(load) / (sum(load) / world),
+                           "_all": (inputs_all, seeds_all)})
     desc, seed, specs = WORKLOADS[name]
     rng = np.random.default_rng(seed)
     inputs = [_input(rng, *s) for s in specs]
@@ -259,6 +256,7 @@ def run_ours(args, rank, world, local_rank, dist):
     torch.cuda.set_device(local_rank)
     lib = N.lib()
     desc, inputs, seeds, total_audio, scaling, extra = make_workload(args.workload, rank, world)
+    all_inputs = extra.pop("_all", None)
     dec = DecodingConfig()
     gen = Generator.synthetic(weight_seed=0, device=local_rank)
 
@@ -315,14 +313,24 @@ def run_ours(args, rank, world, local_rank, dist):
     tflops_peak, hbm_peak, peak_kind = measured_peaks()
     achieved = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else 0.0
 
-    # End to end through the C-ABI with host buffers.
+    # End to end through the public API with host buffers: the C-ABI batch
+    # call per rank; for the batched workload the data-parallel scheduler
+    # (partition on the host, gather of the codes to rank 0).
+    def e2e_once():
+        if all_inputs is None:
+            gen.generate_batch(inputs, dec, seeds, noise=args.noise)
+        else:
+            from omnivoice_b200.scheduler import generate_data_parallel
+            generate_data_parallel(all_inputs[0], dec, all_inputs[1],
+                                   lambda b, d, s: gen.generate_batch(b, d, s, noise=args.noise))
+
     for _ in range(max(1, args.warmup // 2)):
-        gen.generate_batch(inputs, dec, seeds, noise=args.noise)
+        e2e_once()
     barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        gen.generate_batch(inputs, dec, seeds, noise=args.noise)
+        e2e_once()
     torch.cuda.synchronize()
     e2e_s = max_over_ranks(time.perf_counter() - t0)
     st_e2e = gen.stats()
@@ -358,7 +366,9 @@ def run_ours(args, rank, world, local_rank, dist):
         "clocks": clocks.summary(),
         "e2e": {"value": e2e_value, "unit": "audio_s/s",
                 "h2d_bytes_per_step": st_e2e.h2d_bytes, "d2h_bytes_per_step": st_e2e.d2h_bytes,
-                "timing": "wall clock around ov_generator_generate_batch"},
+                "timing": "wall clock around ov_generator_generate_batch"
+                          + (" via omnivoice_b200.scheduler.generate_data_parallel"
+                             if all_inputs is not None else "")},
         "gpu_launches": launches_per_gen * args.steps,
         "kernels": [{k["name"]: round(k["ms"], 4), "launches": k["launches"],
                      "tflops": round(k["flops"] / (k["ms"] / 1e3) / 1e12, 1) if k["flops"] and k["ms"] else None,

@@ -108,12 +108,16 @@ typedef struct {
 /* y (+)= x[rows][in] * w[out][in]^T with float16 operands and float32
  * accumulation in tensor memory (gemm.hpp:41-42, gemm.cpp:248-262).
  * x, w are K-major with row strides ldx / in elements (multiples of 8);
- * y's row stride ldy is in elements of the output type.  `workspace`
- * (optional, may be NULL) enables a deterministic split-K for short-M
- * residual GEMMs: it holds one order counter per output tile
- * (ov_gemm_workspace_bytes gives its size), the splits of a tile add into y
- * in split order.  Zero the workspace once before its first use (every
- * call leaves it zero again); calls sharing a workspace must not overlap. */
+ * y's row stride ldy is in elements of the output type.  Short-M products
+ * with the residual or plain-store epilogue may be split along K across a
+ * thread-block cluster; the splits' partials are summed in split order
+ * through distributed shared memory, so results do not depend on timing.
+ * `workspace` (optional, may be NULL) additionally allows a serialised
+ * split-K: it holds one order counter per output tile
+ * (ov_gemm_workspace_bytes gives its size, 0 when the chosen shape needs
+ * none), the splits of a tile add into y in split order.  Zero the
+ * workspace once before its first use (every call leaves it zero again);
+ * calls sharing a workspace must not overlap. */
 int ov_gemm_f16(const uint16_t* x, size_t ldx, const uint16_t* w, void* y, size_t ldy,
                 size_t rows, size_t in, size_t out, int epilogue,
                 const ov_epilogue_args* args, void* workspace, size_t workspace_bytes,
@@ -145,6 +149,24 @@ int ov_interleave_gate_up(const uint16_t* gate_up, size_t width, size_t in, uint
 int ov_gemm_f16_noalloc(const uint16_t* x, size_t ldx, const uint16_t* w, void* y, size_t ldy,
                         size_t rows, size_t in, size_t out, int epilogue,
                         const ov_epilogue_args* args, ov_stream_t stream);
+
+/* General strided-batched product in the column-major BLAS convention of
+ * HalfGemm::Matmul (gemm.hpp:16-36,56-57): for each batch b,
+ * C_b[m][n] (+)= op(A_b)[m][k] * op(B_b)[k][n], element (i, j) of a
+ * column-major matrix X at x[i + j * ldx], op(X) = X^T when transpose_x.
+ * float16 operands, float32 accumulation and output.  Off the generator's
+ * hot path (a plain CUDA-core kernel); any K and strides. */
+typedef struct {
+  int32_t transpose_a;
+  int32_t transpose_b;
+  size_t m, n, k;
+  size_t lda, ldb, ldc;
+  int64_t stride_a, stride_b, stride_c; /* elements between batches */
+  size_t batch;
+  int32_t accumulate;
+} ov_matmul_shape;
+int ov_matmul_f16(const ov_matmul_shape* shape, const uint16_t* a, const uint16_t* b, float* c,
+                  ov_stream_t stream);
 
 /* ------------------------------------------------------------ attention */
 

@@ -6,7 +6,7 @@ call fails, the functions raise.
 from __future__ import annotations
 
 import ctypes
-from ctypes import (POINTER, Structure, c_char_p, c_float, c_int, c_int32, c_size_t,
+from ctypes import (POINTER, Structure, c_char_p, c_float, c_int, c_int32, c_int64, c_size_t,
                     c_uint16, c_uint32, c_uint64, c_void_p)
 from pathlib import Path
 
@@ -65,6 +65,13 @@ class KernelTime(Structure):
                 ("flops", ctypes.c_double), ("bytes", ctypes.c_double)]
 
 
+class MatmulShape(Structure):
+    _fields_ = [("transpose_a", c_int32), ("transpose_b", c_int32), ("m", c_size_t),
+                ("n", c_size_t), ("k", c_size_t), ("lda", c_size_t), ("ldb", c_size_t),
+                ("ldc", c_size_t), ("stride_a", c_int64), ("stride_b", c_int64),
+                ("stride_c", c_int64), ("batch", c_size_t), ("accumulate", c_int32)]
+
+
 class EpilogueArgs(Structure):
     _fields_ = [("q_norm", c_void_p), ("k_norm", c_void_p), ("positions", c_void_p),
                 ("rope_cos", c_void_p), ("rope_sin", c_void_p), ("max_positions", c_int32),
@@ -114,6 +121,7 @@ SIGNATURES: dict[str, tuple] = {
                             _S, _P]),
     "ov_gemm_workspace_bytes": (c_size_t, [_S, _S, _S, c_int]),
     "ov_interleave_gate_up": (c_int, [_P, _S, _S, _P]),
+    "ov_matmul_f16": (c_int, [POINTER(MatmulShape), _P, _P, _P, _P]),
     "ov_gemm_f16_noalloc": (c_int, [_P, _S, _P, _P, _S, _S, _S, _S, c_int, POINTER(EpilogueArgs),
                                     _P]),
     "ov_attention_varlen": (c_int, [_P, _S, _S, _P, _S, _S, _S, _S, _S, c_float, _P, _S, _P]),

@@ -94,12 +94,38 @@ def build(jobs: int = 0, verbose: bool = False) -> Path:
     return LIBRARY
 
 
+TESTS = ROOT / "tests" / "cpp"
+
+
+def build_test_programs(verbose: bool = False) -> list[Path]:
+    """Links each tests/cpp/*.cpp against the library (run by the GPU tests
+    of the C++ drop-in API); binaries go to omnivoice_b200/_build/."""
+    library = build(verbose=verbose)
+    out = []
+    for src in sorted(TESTS.glob("*.cpp")) if TESTS.exists() else []:
+        exe = BUILD / src.stem
+        out.append(exe)
+        if exe.exists() and exe.stat().st_mtime >= max(src.stat().st_mtime, library.stat().st_mtime):
+            continue
+        cmd = [nvcc(), str(src), "-o", str(exe), "-O2", "-std=c++20", "-I", str(ROOT / "include"),
+               "-I", str(CSRC / "host"), "-L", str(PACKAGE), "-lomnivoice_b200",
+               "-Xlinker", "-rpath=$ORIGIN/.."] + ARCH
+        result = subprocess.run(cmd, capture_output=True, text=True)
+        if verbose or result.returncode != 0:
+            sys.stderr.write(" ".join(cmd) + "\n" + result.stdout + result.stderr)
+        if result.returncode != 0:
+            raise RuntimeError(f"building {src.name} failed")
+    return out
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--jobs", type=int, default=0)
     parser.add_argument("--verbose", action="store_true")
     args = parser.parse_args()
     print(build(args.jobs, args.verbose))
+    for exe in build_test_programs(args.verbose):
+        print(exe)
 
 
 if __name__ == "__main__":

@@ -596,6 +596,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before_sync();
         cluster_sync();
         tc_fence_after_sync();
+        if (c.ep == 0) OV_TRACE(12);
         if (c.ep == 0) {
           const uint32_t slot_bytes = static_cast<uint32_t>(kBM * (BN / args.splits) * 4);
           mbar_arrive_expect_tx(inbox_bar, static_cast<uint32_t>(args.splits - 1) * slot_bytes);
@@ -603,10 +604,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         ClusterSend<BN>(tacc, smem, c, split, args.splits, inbox_bar);
         (void)mbar_wait(inbox_bar, 0, args.err);
         __syncwarp();
+        if (c.ep == 0) OV_TRACE(14);
         ClusterReduce<BN, EPI>(args, &map_y, c, tacc, smem, m_tile, n_tile, split);
+        if (c.ep == 0) OV_TRACE(15);
         // No CTA leaves while a peer's bulk copy may still read its outbox.
         __syncwarp();
         cluster_sync();
+        if (c.ep == 0) OV_TRACE(6);
       }
     }
     if (c.ep == 0) bulk_wait_group<0>();
@@ -1003,6 +1007,11 @@ int ov_gemm_f16_noalloc(const uint16_t* x, size_t ldx, const uint16_t* w, void* 
 }  // extern "C"
 
 #ifdef OV_GEMM_TRACE
+extern "C" int ov_debug_gemm_trace_clear() {
+  static unsigned long long zeros[1024 * 16];
+  return cudaMemcpyToSymbol(ovb::g_gemm_trace, zeros, sizeof(zeros)) == cudaSuccess ? 0 : 2;
+}
+
 extern "C" int ov_debug_gemm_trace(unsigned long long* out, size_t count) {
   return cudaMemcpyFromSymbol(out, ovb::g_gemm_trace, count * sizeof(unsigned long long)) ==
                  cudaSuccess
