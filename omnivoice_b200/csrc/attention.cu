@@ -95,7 +95,9 @@ __device__ __forceinline__ float probs32(const uint32_t (&r)[32], float scale, f
 
 struct AttnArgs {
   const int32_t* cu_seqlens;
-  const int32_t* items;  // [n][2] (sequence, tile pair) or null: blockIdx.y/x
+  // [n][2] work items (sequence, first 128-query tile | max groups << 24),
+  // or null: sequence blockIdx.y, tiles 2 blockIdx.x and 2 blockIdx.x + 1.
+  const int32_t* items;
   __half* out;
   int64_t ld_out;
   int heads;
@@ -108,20 +110,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     attention_kernel(const __grid_constant__ CUtensorMap map_qkv, const AttnArgs args) {
   pdl_wait();
   pdl_trigger();
-  int seq, pair;
+  int seq, tile, max_groups;
   if (args.items != nullptr) {
     seq = args.items[2 * blockIdx.x];
-    pair = args.items[2 * blockIdx.x + 1];
+    const int code = args.items[2 * blockIdx.x + 1];
+    tile = code & 0xFFFFFF;
+    max_groups = code >> 24;
   } else {
     seq = blockIdx.y;
-    pair = blockIdx.x;
+    tile = 2 * blockIdx.x;
+    max_groups = 2;
   }
   const int h = blockIdx.z;
   const int start = args.cu_seqlens[seq];
   const int len = args.cu_seqlens[seq + 1] - start;
-  const int q0 = pair * 2 * kQ;
+  const int q0 = tile * kQ;
   if (q0 >= len) return;  // uniform over the CTA, before any barrier
-  const int groups = q0 + kQ < len ? 2 : 1;
+  const int groups = max_groups >= 2 && q0 + kQ < len ? 2 : 1;
   const int kvh = h / (args.heads / args.kv_heads);
   const int nt = (len + kKeys - 1) / kKeys;
 
@@ -377,8 +382,8 @@ void ConfigureAttentionKernel() {
                     static_cast<int>(kSmemBytes));
 }
 
-// items: device [n_items][2] (sequence, pair of 128-query tiles); null to
-// cover ceil(max_seqlen / 256) pairs of every sequence.
+// items: device [n_items][2] (sequence, first 128-query tile | max groups
+// << 24); null to cover ceil(max_seqlen / 256) tile pairs of every sequence.
 void LaunchAttention(const CUtensorMap& map_qkv, const int32_t* cu_seqlens, int num_seqs,
                      int max_seqlen, const int32_t* items, int n_items, int heads, int kv_heads,
                      float scale, __half* out, int64_t ld_out, cudaStream_t stream) {

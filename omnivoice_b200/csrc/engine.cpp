@@ -308,12 +308,24 @@ void Engine::Prepare(const ov_conditional_input* inputs, size_t count,
   std::stable_sort(seq_order.begin(), seq_order.end(), [&](int32_t a, int32_t b) {
     return cu[a + 1] - cu[a] > cu[b + 1] - cu[b];
   });
+  // A CTA takes two 128-query tiles that share each K/V tile (two softmax
+  // groups ping-ponging on the tensor core) when that still fills the GPU;
+  // short batches take one tile per CTA instead, twice the CTAs.
+  size_t pairs = 0, singles = 0;
+  for (size_t q = 0; q < n_seqs_; ++q) {
+    const size_t len = static_cast<size_t>(cu[q + 1] - cu[q]);
+    pairs += (len + 255) / 256;
+    singles += (len + 127) / 128;
+  }
+  const bool single_tiles = pairs * cfg_.heads < static_cast<size_t>(sms_) &&
+                            singles * cfg_.heads <= 2 * static_cast<size_t>(sms_);
+  const int32_t per_item = single_tiles ? 1 : 2;
   std::vector<int32_t> items;
   for (const int32_t q : seq_order) {
     const int32_t len = cu[q + 1] - cu[q];
-    for (int32_t pair = 0; pair * 256 < len; ++pair) {
+    for (int32_t tile = 0; tile * 128 < len; tile += per_item) {
       items.push_back(q);
-      items.push_back(pair);
+      items.push_back(tile | (per_item << 24));
     }
   }
   n_items_ = items.size() / 2;

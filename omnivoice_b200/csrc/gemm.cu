@@ -47,7 +47,7 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // producer warp, MMA warp, 8 epilogue warps
 constexpr int kRingBytes = 196608;
 constexpr uint32_t kStageTile = 128 * 128;  // one staging tile: 128 rows x 128 bytes
 constexpr int kGroupM = 8;                  // rasterisation group of m tiles
@@ -99,23 +99,38 @@ __device__ __forceinline__ void UnitCoords(const GemmArgs& a, int u, int& m_tile
   m_tile = first_m + local % gm;
 }
 
-// Epilogue state shared by the 128 epilogue threads.
+// Epilogue state.  Eight epilogue warps form two groups of four; each
+// group has one thread per tile row (tensor-memory lane) and the groups
+// split each tile's columns, so every SM sub-partition runs two epilogue
+// warps.
 struct EpilogueCtx {
   uint8_t* staging;      // 2 x kStageTile, 1024-byte aligned
-  uint32_t chunk_iter;   // staging buffer alternation
-  int ep;                // 0..127
+  uint32_t chunk_iter;   // chunks this group staged (non-ring mode)
+  uint32_t joint_iter;   // chunks both groups staged together (non-ring mode)
+  int ep;                // 0..255
+  int gep;               // 0..127: index within the group; 0 leads the group
+  int group;             // 0 or 1
   int row;               // tile row = tensor-memory lane
+  // Last unit of this CTA: the operand ring is idle (every load consumed,
+  // every MMA complete), so each chunk takes its own kStageTile slot of it
+  // and no chunk waits for an earlier store to drain.
+  uint8_t* ring;         // nullptr: stage through the two staging tiles
 };
 
-// RoPE cos / sin of one row's position (QK-norm epilogue), loaded before
-// the accumulator is ready so the loads overlap the tile's MMAs.
+constexpr uint32_t kGroupBarrier = 1;  // + group: the 128 threads of a group
+constexpr uint32_t kEpiBarrier = 3;    // all 256 epilogue threads
+
+// RoPE cos / sin of one row's position for the 32 rotated pairs this
+// group computes (QK-norm epilogue), loaded before the accumulator is
+// ready so the loads overlap the tile's MMAs.
 struct RopeRow {
-  float4 c[16];
-  float4 s[16];
+  float4 c[8];
+  float4 s[8];
 };
 
 template <int EPI>
-__device__ __forceinline__ void LoadRopeRow(const GemmArgs& a, int m_tile, int row, RopeRow& r) {
+__device__ __forceinline__ void LoadRopeRow(const GemmArgs& a, int m_tile, int row, int group,
+                                            RopeRow& r) {
   if constexpr (EPI == OV_EPI_QKNORM_ROPE_F16) {
     const int64_t grow = static_cast<int64_t>(m_tile) * kBM + row;
     int pos = grow < a.M ? __ldg(a.positions + grow) : 0;
@@ -123,10 +138,12 @@ __device__ __forceinline__ void LoadRopeRow(const GemmArgs& a, int m_tile, int r
       atomicOr(a.err, kErrBadArgument);
       pos = 0;
     }
-    const float4* cs = reinterpret_cast<const float4*>(a.rope_cos + static_cast<int64_t>(pos) * 64);
-    const float4* sn = reinterpret_cast<const float4*>(a.rope_sin + static_cast<int64_t>(pos) * 64);
+    const float4* cs =
+        reinterpret_cast<const float4*>(a.rope_cos + static_cast<int64_t>(pos) * 64) + 8 * group;
+    const float4* sn =
+        reinterpret_cast<const float4*>(a.rope_sin + static_cast<int64_t>(pos) * 64) + 8 * group;
 #pragma unroll
-    for (int k = 0; k < 16; ++k) {
+    for (int k = 0; k < 8; ++k) {
       r.c[k] = __ldg(cs + k);
       r.s[k] = __ldg(sn + k);
     }
@@ -137,22 +154,29 @@ __device__ __forceinline__ float F4At(const float4& v, int i) {
   return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
 }
 
-// Writes this thread's 128-byte row piece into the next staging tile and
-// has one thread store (or reduce-add) the tile at column x, row y0.
+// One group writes its threads' 128-byte row pieces into a staging tile
+// (ring slot `slot`, or the group's staging tile) and the group leader
+// stores (or reduce-adds) the tile at column x, row y0.
 template <bool kReduce>
-__device__ __forceinline__ void EmitChunk(EpilogueCtx& c, const CUtensorMap* map,
-                                          const uint32_t (&w)[32], int x, int y0) {
-  uint8_t* buf = c.staging + (c.chunk_iter & 1u) * kStageTile;
-  if (c.chunk_iter >= 2 && c.ep == 0) bulk_wait_group_read<1>();
-  named_barrier(1, 128);  // the staging tile is free again
+__device__ __forceinline__ void EmitGroup(EpilogueCtx& c, const CUtensorMap* map,
+                                          const uint32_t (&w)[32], int x, int y0, int slot) {
+  uint8_t* buf;
+  const uint32_t bar = kGroupBarrier + static_cast<uint32_t>(c.group);
+  if (c.ring != nullptr) {
+    buf = c.ring + slot * kStageTile;
+  } else {
+    buf = c.staging + c.group * kStageTile;
+    if (c.chunk_iter > 0 && c.gep == 0) bulk_wait_group_read<0>();
+    named_barrier(bar, 128);  // the group's staging tile is free again
+  }
   uint8_t* dst = buf + c.row * 128;
 #pragma unroll
   for (int q = 0; q < 8; ++q)
     *reinterpret_cast<uint4*>(dst + ((q ^ (c.row & 7)) << 4)) =
         make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
   fence_proxy_async_smem();
-  named_barrier(1, 128);
-  if (c.ep == 0) {
+  named_barrier(bar, 128);
+  if (c.gep == 0) {
     if (kReduce)
       tma_reduce_add_2d(map, buf, x, y0);
     else
@@ -162,6 +186,32 @@ __device__ __forceinline__ void EmitChunk(EpilogueCtx& c, const CUtensorMap* map
   ++c.chunk_iter;
 }
 
+// Both groups fill one staging tile, group g the 64-byte half g of every
+// row piece (16 words); thread 0 stores it at column x, row y0.
+__device__ __forceinline__ void EmitJoint(EpilogueCtx& c, const CUtensorMap* map,
+                                          const uint32_t (&w)[16], int x, int y0, int slot) {
+  uint8_t* buf;
+  if (c.ring != nullptr) {
+    buf = c.ring + slot * kStageTile;
+  } else {
+    buf = c.staging + (c.joint_iter & 1u) * kStageTile;
+    if (c.joint_iter >= 2 && c.ep == 0) bulk_wait_group_read<1>();
+    named_barrier(kEpiBarrier, 256);
+  }
+  uint8_t* dst = buf + c.row * 128;
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    *reinterpret_cast<uint4*>(dst + (((4 * c.group + q) ^ (c.row & 7)) << 4)) =
+        make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+  fence_proxy_async_smem();
+  named_barrier(kEpiBarrier, 256);
+  if (c.ep == 0) {
+    tma_store_2d(map, buf, x, y0);
+    bulk_commit_group();
+  }
+  ++c.joint_iter;
+}
+
 template <int BN, int EPI>
 __device__ __forceinline__ void EpilogueUnit(const GemmArgs& a, const CUtensorMap* map_y,
                                              EpilogueCtx& c, uint32_t tacc, int m_tile,
@@ -169,21 +219,62 @@ __device__ __forceinline__ void EpilogueUnit(const GemmArgs& a, const CUtensorMa
                                              const RopeRow& rope) {
   const int y0 = m_tile * kBM;
   if constexpr (EPI == OV_EPI_STORE_F32 || EPI == OV_EPI_ACCUM_F32) {
+    // 32-column chunks; group g takes the chunks k with k % 2 == g.
+    const int chunks = min(BN, a.out_cols - n_tile * BN + 31) / 32;  // >= 1
+    if (c.ring != nullptr) {
+      // Each chunk into its own ring slot, the tensor-memory load of the
+      // group's next chunk in flight while this one is written; one
+      // barrier, then the group leader issues the group's stores.
+      const uint32_t bar = kGroupBarrier + static_cast<uint32_t>(c.group);
+      uint32_t r[2][32];
+      int issued = 0;
+      if (c.group < chunks) {
+        tmem_ld_32x32b_x32(tacc + c.group * 32, r[0]);
+        tmem_ld_wait();
+      }
+#pragma unroll
+      for (int i = 0; i < BN / 64; ++i) {
+        const int k = 2 * i + c.group;
+        if (k >= chunks) break;  // uniform over the group
+        const int kn = k + 2;
+        if (kn < chunks) tmem_ld_32x32b_x32(tacc + kn * 32, r[(i + 1) & 1]);
+        uint8_t* dst = c.ring + k * kStageTile + c.row * 128;
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          *reinterpret_cast<uint4*>(dst + ((q ^ (c.row & 7)) << 4)) =
+              make_uint4(r[i & 1][4 * q], r[i & 1][4 * q + 1], r[i & 1][4 * q + 2],
+                         r[i & 1][4 * q + 3]);
+        ++issued;
+        if (kn < chunks) tmem_ld_wait();
+      }
+      fence_proxy_async_smem();
+      named_barrier(bar, 128);
+      if (c.gep == 0 && issued > 0) {
+        for (int k = c.group; k < chunks; k += 2) {
+          const uint8_t* buf = c.ring + k * kStageTile;
+          if (EPI == OV_EPI_ACCUM_F32)
+            tma_reduce_add_2d(map_y, buf, n_tile * BN + k * 32, y0);
+          else
+            tma_store_2d(map_y, buf, n_tile * BN + k * 32, y0);
+        }
+        bulk_commit_group();
+      }
+    } else {
 #pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 32) {
-      const int x = n_tile * BN + c0;
-      if (x >= a.out_cols) break;  // uniform over the epilogue threads
-      uint32_t r[32];
-      tmem_ld_32x32b_x32(tacc + c0, r);
-      tmem_ld_wait();
-      EmitChunk<EPI == OV_EPI_ACCUM_F32>(c, map_y, r, x, y0);
+      for (int k = c.group; k < chunks; k += 2) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tacc + k * 32, r);
+        tmem_ld_wait();
+        EmitGroup<EPI == OV_EPI_ACCUM_F32>(c, map_y, r, n_tile * BN + k * 32, y0, k);
+      }
     }
   } else if constexpr (EPI == OV_EPI_SWIGLU_F16) {
     // The tile holds BN / 128 groups of [64 gate | 64 up] columns; each
-    // group gives 64 half outputs = one 128-byte row piece.
+    // gives 64 half outputs = one 128-byte row piece.  Epilogue group g
+    // takes the gate/up groups gi with gi % 2 == g.
     constexpr int G = OV_SWIGLU_GROUP;
 #pragma unroll 1
-    for (int gi = 0; gi < BN / (2 * G); ++gi) {
+    for (int gi = c.group; gi < BN / (2 * G); gi += 2) {
       uint32_t out[32];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
@@ -197,14 +288,15 @@ __device__ __forceinline__ void EpilogueUnit(const GemmArgs& a, const CUtensorMa
               pack_half2(silu_mul(__uint_as_float(g[j]), __uint_as_float(u[j])),
                          silu_mul(__uint_as_float(g[j + 1]), __uint_as_float(u[j + 1])));
       }
-      EmitChunk<false>(c, map_y, out, n_tile * (BN / 2) + gi * G, y0);
+      EmitGroup<false>(c, map_y, out, n_tile * (BN / 2) + gi * G, y0, gi);
     }
   } else if constexpr (EPI == OV_EPI_QKNORM_ROPE_F16) {
-    // BN / 128 heads per tile.  Tensor memory is read in 16-column pieces,
-    // several times over (RMS first, then the low and the high half of the
-    // rotated pairs (i, i + 64)), so a thread never holds more than one
-    // output row piece besides its RoPE row.
+    // BN / 128 heads per tile.  Group g computes the rotated pairs
+    // (i, i + 64) for i in [32 g, 32 g + 32) of every head: the low 64-byte
+    // half (g = 0) or the high half (g = 1) of both output row pieces.
+    // Each group reads the whole head once for its RMS.
     static_assert(BN % 128 == 0, "whole heads per tile");
+    const int i_base = 32 * c.group;
 #pragma unroll 1
     for (int hh = 0; hh < BN / 128; ++hh) {
       const int slot = n_tile * (BN / 128) + hh;
@@ -221,52 +313,52 @@ __device__ __forceinline__ void EpilogueUnit(const GemmArgs& a, const CUtensorMa
           for (int j = 0; j < 16; ++j) ss = fmaf(__uint_as_float(r[j]), __uint_as_float(r[j]), ss);
         }
         const float scale = 1.0f / sqrtf(ss / 128.0f + a.epsilon);
+        uint32_t lo[16], hi[16];
 #pragma unroll
-        for (int part = 0; part < 2; ++part) {  // 0: columns 0..63, 1: 64..127
-          uint32_t out[32];
+        for (int b = 0; b < 2; ++b) {  // pairs i_base + 16 b .. + 15
+          const int i0 = i_base + 16 * b;
+          uint32_t r1[16], r2[16];
+          tmem_ld_32x32b_x16(th + i0, r1);
+          tmem_ld_32x32b_x16(th + 64 + i0, r2);
+          tmem_ld_wait();
 #pragma unroll
-          for (int i0 = 0; i0 < 64; i0 += 16) {
-            uint32_t r1[16], r2[16];
-            tmem_ld_32x32b_x16(th + i0, r1);
-            tmem_ld_32x32b_x16(th + 64 + i0, r2);
-            tmem_ld_wait();
+          for (int i4 = 0; i4 < 4; ++i4) {
+            const float4 w14 = lds_in_order(w + i0 + i4 * 4);
+            const float4 w24 = lds_in_order(w + 64 + i0 + i4 * 4);
+            float l4[4], h4[4];
 #pragma unroll
-            for (int i4 = 0; i4 < 4; ++i4) {
-              const float4 w14 = lds_in_order(w + i0 + i4 * 4);
-              const float4 w24 = lds_in_order(w + 64 + i0 + i4 * 4);
-              float o4[4];
-#pragma unroll
-              for (int t = 0; t < 4; ++t) {
-                const int i = i0 + i4 * 4 + t;
-                const float cc = F4At(rope.c[i / 4], t);
-                const float sn = F4At(rope.s[i / 4], t);
-                const float x1 = F4At(w14, t) * (__uint_as_float(r1[i4 * 4 + t]) * scale);
-                const float x2 = F4At(w24, t) * (__uint_as_float(r2[i4 * 4 + t]) * scale);
-                o4[t] = part == 0 ? __fsub_rn(__fmul_rn(x1, cc), __fmul_rn(x2, sn))
-                                  : __fadd_rn(__fmul_rn(x2, cc), __fmul_rn(x1, sn));
-              }
-              out[i0 / 2 + i4 * 2] = pack_half2(o4[0], o4[1]);
-              out[i0 / 2 + i4 * 2 + 1] = pack_half2(o4[2], o4[3]);
+            for (int t = 0; t < 4; ++t) {
+              const int k = 4 * b + i4;  // RopeRow index of pair i0 + 4 i4 + t
+              const float cc = F4At(rope.c[k], t);
+              const float sn = F4At(rope.s[k], t);
+              const float x1 = F4At(w14, t) * (__uint_as_float(r1[i4 * 4 + t]) * scale);
+              const float x2 = F4At(w24, t) * (__uint_as_float(r2[i4 * 4 + t]) * scale);
+              l4[t] = __fsub_rn(__fmul_rn(x1, cc), __fmul_rn(x2, sn));
+              h4[t] = __fadd_rn(__fmul_rn(x2, cc), __fmul_rn(x1, sn));
             }
+            const int o = 8 * b + 2 * i4;
+            lo[o] = pack_half2(l4[0], l4[1]);
+            lo[o + 1] = pack_half2(l4[2], l4[3]);
+            hi[o] = pack_half2(h4[0], h4[1]);
+            hi[o + 1] = pack_half2(h4[2], h4[3]);
           }
-          EmitChunk<false>(c, map_y, out, slot * 128 + part * 64, y0);
         }
+        EmitJoint(c, map_y, lo, slot * 128, y0, 2 * hh);
+        EmitJoint(c, map_y, hi, slot * 128 + 64, y0, 2 * hh + 1);
       } else {
-        // v heads: plain half conversion.
+        // v heads: plain half conversion of this group's columns.
+        uint32_t lo[16], hi[16];
+        uint32_t r1[32], r2[32];
+        tmem_ld_32x32b_x32(th + i_base, r1);
+        tmem_ld_32x32b_x32(th + 64 + i_base, r2);
+        tmem_ld_wait();
 #pragma unroll
-        for (int part = 0; part < 2; ++part) {
-          uint32_t out[32];
-#pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            uint32_t r[32];
-            tmem_ld_32x32b_x32(th + part * 64 + q * 32, r);
-            tmem_ld_wait();
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-              out[q * 16 + j] = pack_half2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
-          }
-          EmitChunk<false>(c, map_y, out, slot * 128 + part * 64, y0);
+        for (int j = 0; j < 16; ++j) {
+          lo[j] = pack_half2(__uint_as_float(r1[2 * j]), __uint_as_float(r1[2 * j + 1]));
+          hi[j] = pack_half2(__uint_as_float(r2[2 * j]), __uint_as_float(r2[2 * j + 1]));
         }
+        EmitJoint(c, map_y, lo, slot * 128, y0, 2 * hh);
+        EmitJoint(c, map_y, hi, slot * 128 + 64, y0, 2 * hh + 1);
       }
     }
   }
@@ -281,22 +373,24 @@ __device__ __forceinline__ void EpilogueUnit(const GemmArgs& a, const CUtensorMa
 // Slot of rank `other` among the S - 1 ranks other than `self`.
 __device__ __forceinline__ int PeerSlot(int other, int self) { return other < self ? other : other - 1; }
 
-// Step 1 (epilogue thread `row`): every other rank's slice of this CTA's
-// partial goes from tensor memory into the outbox; then one thread sends
-// each outbox slot to its rank's inbox with a bulk copy that completes on
-// that rank's inbox barrier.
+// Step 1: every other rank's slice of this CTA's partial goes from tensor
+// memory into the outbox (the two epilogue groups take alternate 32-column
+// chunks); then one thread sends each outbox slot to its rank's inbox with
+// a bulk copy that completes on that rank's inbox barrier.
 template <int BN>
 __device__ __forceinline__ void ClusterSend(uint32_t tacc, uint8_t* ring, const EpilogueCtx& c,
                                             int rank, int splits, uint64_t* inbox_bar) {
   const int cols = BN / splits;
   const uint32_t slot_bytes = static_cast<uint32_t>(kBM * cols * 4);
   uint8_t* outbox = ring + (splits - 1) * slot_bytes;
+  int chunk = 0;
 #pragma unroll 1
   for (int j = 0; j < splits; ++j) {
     if (j == rank) continue;
     uint8_t* slot = outbox + PeerSlot(j, rank) * slot_bytes;
 #pragma unroll 1
-    for (int cc = 0; cc < cols; cc += 32) {
+    for (int cc = 0; cc < cols; cc += 32, ++chunk) {
+      if ((chunk & 1) != c.group) continue;  // uniform over the group
       uint32_t v[32];
       tmem_ld_32x32b_x32(tacc + static_cast<uint32_t>(j * cols + cc), v);
       tmem_ld_wait();
@@ -308,7 +402,7 @@ __device__ __forceinline__ void ClusterSend(uint32_t tacc, uint8_t* ring, const 
     }
   }
   fence_proxy_async_smem();
-  named_barrier(1, 128);
+  named_barrier(kEpiBarrier, 256);
   if (c.ep == 0) {
     const uint32_t inbox = smem_u32(ring);
     for (int j = 0; j < splits; ++j) {
@@ -322,7 +416,8 @@ __device__ __forceinline__ void ClusterSend(uint32_t tacc, uint8_t* ring, const 
 
 // Step 2: this rank's slice is the sum of the splits' partials in split
 // order (its own from tensor memory, the others from the inbox), stored or
-// added into y like an unsplit tile.
+// added into y like an unsplit tile; group g takes the chunks cc / 32 with
+// the parity g.
 template <int BN, int EPI>
 __device__ __forceinline__ void ClusterReduce(const GemmArgs& a, const CUtensorMap* map_y,
                                               EpilogueCtx& c, uint32_t tacc, const uint8_t* ring,
@@ -332,9 +427,9 @@ __device__ __forceinline__ void ClusterReduce(const GemmArgs& a, const CUtensorM
   const int slot_bytes = kBM * cols * 4;
   const int y0 = m_tile * kBM;
 #pragma unroll 1
-  for (int cc = 0; cc < cols; cc += 32) {
+  for (int cc = 32 * c.group; cc < cols; cc += 64) {
     const int x = n_tile * BN + rank * cols + cc;
-    if (x >= a.out_cols) break;  // uniform over the epilogue threads
+    if (x >= a.out_cols) break;  // uniform over the group
     float acc[32];
 #pragma unroll
     for (int e = 0; e < 32; ++e) acc[e] = 0.0f;
@@ -361,7 +456,7 @@ __device__ __forceinline__ void ClusterReduce(const GemmArgs& a, const CUtensorM
     uint32_t w[32];
 #pragma unroll
     for (int e = 0; e < 32; ++e) w[e] = __float_as_uint(acc[e]);
-    EmitChunk<EPI == OV_EPI_ACCUM_F32>(c, map_y, w, x, y0);
+    EmitGroup<EPI == OV_EPI_ACCUM_F32>(c, map_y, w, x, y0, 0);
   }
 }
 
@@ -409,7 +504,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 128);
+      mbar_init(&tempty[b], 256);
     }
     mbar_init(inbox_bar, 1);
     fence_mbar_init();
@@ -423,9 +518,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if constexpr (EPI == OV_EPI_QKNORM_ROPE_F16) {
     if (warp >= 2) {
-      const int i = threadIdx.x - 64;
-      norm_w[i] = args.q_norm[i];
-      norm_w[128 + i] = args.k_norm[i];
+      const int i = threadIdx.x - 64;  // 0..255: q_norm then k_norm
+      norm_w[i] = i < 128 ? args.q_norm[i] : args.k_norm[i - 128];
     }
   }
   tc_fence_before_sync();
@@ -545,7 +639,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     EpilogueCtx c;
     c.staging = staging;
     c.chunk_iter = 0;
+    c.joint_iter = 0;
+    c.ring = nullptr;
     c.ep = threadIdx.x - 64;
+    c.group = c.ep >> 7;
+    c.gep = c.ep & 127;
     const int quarter = warp & 3;  // tensor-memory lanes 32*quarter .. +31
     c.row = quarter * 32 + lane;
     int acc_iter = 0;
@@ -554,34 +652,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       UnitCoords(args, u, m_tile, n_tile, split);
       const int buf = acc_iter & 1;
       RopeRow rope;
-      LoadRopeRow<EPI>(args, m_tile, c.row, rope);
+      LoadRopeRow<EPI>(args, m_tile, c.row, c.group, rope);
       // Every epilogue thread runs the epilogue even after a timed-out wait
-      // (the error word is set) so the 128 threads stay in step.
+      // (the error word is set) so the 256 threads stay in step.
       (void)mbar_wait(&tfull[buf], static_cast<uint32_t>(acc_iter >> 1) & 1u, args.err);
       __syncwarp();  // the tensor-memory loads below are warp-collective
       if (acc_iter == 0 && c.ep == 0) OV_TRACE(5);
       tc_fence_after_sync();
       if (args.cluster) break;  // one unit per CTA, reduced below
       const int tile = u / args.splits;
-      if (EPI == OV_EPI_ACCUM_F32 && args.splits > 1 && c.ep == 0) {
+      if (EPI == OV_EPI_ACCUM_F32 && args.splits > 1) {
         // Earlier splits of this tile first; their adds are complete.
-        (void)wait_counter_equals(args.counters + tile, static_cast<uint32_t>(split), args.err);
-        fence_proxy_async_global();
-        if (acc_iter == 0) OV_TRACE(12);
+        if (c.ep == 0) {
+          (void)wait_counter_equals(args.counters + tile, static_cast<uint32_t>(split), args.err);
+          if (acc_iter == 0) OV_TRACE(12);
+        }
+        named_barrier(kEpiBarrier, 256);
+        if (c.gep == 0) fence_proxy_async_global();
       }
       const uint32_t tacc =
           tmem + static_cast<uint32_t>(buf * BN) + (static_cast<uint32_t>(quarter * 32) << 16);
+      // This CTA's last unit: its loads are all consumed and its MMAs done.
+      c.ring = u + static_cast<int>(gridDim.x) >= args.units ? smem : nullptr;
       EpilogueUnit<BN, EPI>(args, &map_y, c, tacc, m_tile, n_tile, norm_w, rope);
       tc_fence_before_sync();
       mbar_arrive(&tempty[buf]);
-      if (EPI == OV_EPI_ACCUM_F32 && args.splits > 1 && c.ep == 0) {
-        bulk_wait_group<0>();
-        fence_proxy_async_global();
-        __threadfence();
-        if (split == args.splits - 1)
-          st_relaxed_gpu(args.counters + tile, 0u);  // ready for the next launch
-        else
-          red_release_gpu_add(args.counters + tile, 1u);
+      if (EPI == OV_EPI_ACCUM_F32 && args.splits > 1) {
+        if (c.gep == 0) {  // both group leaders: their adds are complete
+          bulk_wait_group<0>();
+          fence_proxy_async_global();
+        }
+        named_barrier(kEpiBarrier, 256);
+        if (c.ep == 0) {
+          __threadfence();
+          if (split == args.splits - 1)
+            st_relaxed_gpu(args.counters + tile, 0u);  // ready for the next launch
+          else
+            red_release_gpu_add(args.counters + tile, 1u);
+        }
       }
       if (acc_iter == 0 && c.ep == 0) OV_TRACE(6);
     }
@@ -613,7 +721,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (c.ep == 0) OV_TRACE(6);
       }
     }
-    if (c.ep == 0) bulk_wait_group<0>();
+    if (c.gep == 0) bulk_wait_group<0>();  // each group leader's stores
 #ifdef OV_GEMM_TRACE
     if (c.ep == 0) {
       OV_TRACE(7);
