@@ -48,7 +48,8 @@ constexpr int kD = 128;        // head dim
 constexpr int kThreads = 320;  // 2 softmax groups + producer + MMA warp
 constexpr uint32_t kHalfTile = 128 * 64 * 2;  // one [128][64] half box: 16 KB
 constexpr uint32_t kTile = 2 * kHalfTile;     // [128][128] half: 32 KB
-constexpr uint32_t kSmemBytes = 2 * kTile /*Q0,Q1*/ + 2 * 2 * kTile /*K,V ring*/ + 1024 + 256;
+// Q0, Q1 | K, V ring of two stages | barriers, row-statistics exchange.
+constexpr uint32_t kSmemBytes = 2 * kTile + 2 * 2 * kTile + 1024 + 4096;
 constexpr float kRescaleThreshold = 8.0f;     // log2 units: P stays below 2^8
 
 // 2^x by the MUFU instruction (relative error far below the half rounding
@@ -93,6 +94,19 @@ __device__ __forceinline__ float probs32(const uint32_t (&r)[32], float scale, f
   return a + b;
 }
 
+#ifdef OV_ATTN_TRACE
+// Timing probe of a diagnostic build: %globaltimer at milestones per CTA
+// (compiled only with -DOV_ATTN_TRACE).
+__device__ unsigned long long g_attn_trace[4096 * 8];
+#define OV_ATRACE(slot)                                                          \
+  g_attn_trace[(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z)) % 4096 * 8 + \
+               (slot)] = global_timer_ns()
+#else
+#define OV_ATRACE(slot) \
+  do {                  \
+  } while (0)
+#endif
+
 struct AttnArgs {
   const int32_t* cu_seqlens;
   // [n][2] work items (sequence, first 128-query tile | max groups << 24),
@@ -106,8 +120,205 @@ struct AttnArgs {
   uint32_t* err;
 };
 
+// The softmax warpgroups' part of attention_kernel (see there); kSplit:
+// one query tile shared by both warpgroups.
+template <bool kSplit>
+__device__ __forceinline__ void SoftmaxRole(const AttnArgs& args, const CUtensorMap* map_out_p,
+                                            uint32_t tmem, uint64_t* s_full, uint64_t* p_full,
+                                            uint64_t* o_done, uint64_t* pv_done, float* xmax,
+                                            float* xsum,
+                                            uint8_t* q_s, int warp, int lane, int len, int nt,
+                                            int q0, int start, int h) {
+  // Softmax warpgroups (warps 0-3: wg 0, warps 4-7: wg 1); a thread owns
+  // one query row (tensor-memory lane).  With two query tiles warpgroup g
+  // owns tile g (S/P and O regions g).  With one tile both share it
+  // ("split"): warpgroup wg takes key columns [64 wg, 64 wg + 64) of every
+  // S tile and O columns [64 wg, 64 wg + 64), and the two halves of a row
+  // meet in shared memory for the row maximum and the row sum.
+  constexpr bool split = kSplit;
+  const int wg = warp >> 2;
+  const int g = split ? 0 : wg;
+  const int row = (warp & 3) * 32 + lane;
+  const int col0 = split ? 64 * wg : 0;  // first key column and first O column
+  constexpr int halves = split ? 1 : 2;  // 64-column halves handled
+  const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+  const uint32_t o_addr = tmem + static_cast<uint32_t>(g * 256 + 128) + lane_off;
+  float m = -INFINITY, l = 0.0f;
+  // A timed-out wait (error word set) does not end the loop: every warp
+  // keeps meeting the named barriers of the split tile and of the epilogue.
+  for (int t = 0; t < nt; ++t) {
+    // Split: S(t) in region t & 1 (two phases per region); else region g.
+    const int sb = split ? (t & 1) : g;
+    const uint32_t sphase = split ? static_cast<uint32_t>(t >> 1) & 1u : static_cast<uint32_t>(t) & 1u;
+    const uint32_t s_addr = tmem + static_cast<uint32_t>(sb * 256) + lane_off;
+    (void)mbar_wait(&s_full[sb], sphase, args.err);
+    __syncwarp();  // the tensor-memory accesses below are warp-collective
+    tc_fence_after_sync();
+    const int valid = min(kKeys, len - t * kKeys);
+    // Pass 1: row maximum (two 32-column chunks in registers at a time;
+    // keys past the sequence end read as -inf).
+    float mt = -INFINITY;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      if (half >= halves) break;  // uniform over the CTA
+      const int k0 = col0 + half * 64;
+      uint32_t ra[32], rb[32];
+      tmem_ld_32x32b_x32(s_addr + k0, ra);
+      tmem_ld_32x32b_x32(s_addr + k0 + 32, rb);
+      tmem_ld_wait();
+      if (valid < kKeys) {
+        mask_keys(ra, k0, valid);
+        mask_keys(rb, k0 + 32, valid);
+      }
+      mt = fmaxf(mt, fmaxf(max32(ra), max32(rb)));
+    }
+    if (split) {
+      float* xm = xmax + (t & 1) * 256;
+      xm[wg * 128 + row] = mt;
+      named_barrier(1, 256);
+      mt = fmaxf(xm[row], xm[128 + row]);
+    }
+    mt *= args.scale_log2;
+    if (t == 0) {
+      m = mt;
+    } else {
+      // tcgen05.ld / st are warp-collective (.sync.aligned): the whole
+      // warp rescales when any of its rows needs it; rows whose maximum
+      // did not grow past the threshold keep theirs (alpha = 1).  Both
+      // warpgroups of a split tile see the same maxima, so they decide
+      // alike and each rescales its own O columns.
+      const bool grow = mt > m + kRescaleThreshold;
+      if (__any_sync(0xFFFFFFFFu, grow)) {
+        // Two tiles: the previous P V of this tile completed before S_t was
+        // written (one thread issues both, in order), so O is stable here.
+        // Split: S(t) may have run before P V(t - 1); wait for it.
+        if (split) {
+          (void)mbar_wait(pv_done, static_cast<uint32_t>(t - 1) & 1u, args.err);
+          __syncwarp();
+          tc_fence_after_sync();
+        }
+        const float m_new = grow ? mt : m;
+        const float alpha = ex2_approx(m - m_new);
+        l *= alpha;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          if (c >= 2 * halves) break;  // uniform over the CTA
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(o_addr + col0 + c * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * alpha);
+          tmem_st_32x32b_x16(o_addr + col0 + c * 32,
+                             *reinterpret_cast<const uint32_t(*)[16]>(&r[0]));
+          tmem_st_32x32b_x16(o_addr + col0 + c * 32 + 16,
+                             *reinterpret_cast<const uint32_t(*)[16]>(&r[16]));
+        }
+        m = m_new;
+      }
+    }
+    // Pass 2: probabilities, written as half pairs over the consumed S
+    // columns (key k -> column k / 2).
+    float rowsum = 0.0f;
+    const float neg_m = -m;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      if (half >= halves) break;  // uniform over the CTA
+      const int k0 = col0 + half * 64;
+      uint32_t ra[32], rb[32];
+      tmem_ld_32x32b_x32(s_addr + k0, ra);
+      tmem_ld_32x32b_x32(s_addr + k0 + 32, rb);
+      tmem_ld_wait();
+      if (valid < kKeys) {
+        mask_keys(ra, k0, valid);
+        mask_keys(rb, k0 + 32, valid);
+      }
+      uint32_t pa[16], pb[16];
+      rowsum += probs32(ra, args.scale_log2, neg_m, pa);
+      rowsum += probs32(rb, args.scale_log2, neg_m, pb);
+      tmem_st_32x32b_x16(s_addr + k0 / 2, pa);
+      tmem_st_32x32b_x16(s_addr + k0 / 2 + 16, pb);
+    }
+    l += rowsum;
+    tmem_st_wait();
+    tc_fence_before_sync();
+    mbar_arrive(&p_full[sb]);
+    if (threadIdx.x == 0 && t == 0) OV_ATRACE(3);
+    if (threadIdx.x == 0 && t == nt - 1) OV_ATRACE(4);
+  }
+  if (split) {  // row sum = half 0 + half 1
+    xsum[wg * 128 + row] = l;
+    named_barrier(1, 256);
+    l = xsum[row] + xsum[128 + row];
+  }
+  (void)mbar_wait(&o_done[g], 0, args.err);
+  __syncwarp();
+  {
+    if (threadIdx.x == 0) OV_ATRACE(5);
+    tc_fence_after_sync();
+    const float inv = 1.0f / l;
+    const int tile_row0 = q0 + g * kQ;
+    if (tile_row0 + kQ <= len) {
+      // Whole tile: O (half) through the tile's Q buffer, idle since its
+      // last S MMA, as 128B-swizzled [128][64] boxes, one TMA store each.
+      uint8_t* stage = q_s + g * kTile;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        if (c >= 2 * halves) break;  // uniform over the CTA
+        const int ocol = col0 + c * 32;  // output column of this chunk
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(o_addr + ocol, r);
+        tmem_ld_wait();
+        uint8_t* dst = stage + (ocol >> 6) * kHalfTile + row * 128;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int piece = ((ocol & 63) >> 3) + q;  // 16-byte piece within the 128-byte row
+          *reinterpret_cast<uint4*>(dst + ((piece ^ (row & 7)) << 4)) =
+              make_uint4(pack_half2(__uint_as_float(r[8 * q]) * inv, __uint_as_float(r[8 * q + 1]) * inv),
+                         pack_half2(__uint_as_float(r[8 * q + 2]) * inv, __uint_as_float(r[8 * q + 3]) * inv),
+                         pack_half2(__uint_as_float(r[8 * q + 4]) * inv, __uint_as_float(r[8 * q + 5]) * inv),
+                         pack_half2(__uint_as_float(r[8 * q + 6]) * inv, __uint_as_float(r[8 * q + 7]) * inv));
+        }
+      }
+      fence_proxy_async_smem();
+      named_barrier(2 + wg, 128);
+      if ((warp & 3) == 0 && lane == 0) {
+        for (int b = col0 >> 6; b < (col0 >> 6) + halves; ++b)
+          tma_store_2d(map_out_p, stage + b * kHalfTile, h * kD + b * 64, start + tile_row0);
+        bulk_commit_group();
+        bulk_wait_group_read<0>();  // staging read; the writes complete with the grid
+      }
+    } else {
+      // Last, partial tile of a sequence: rows past its end belong to the
+      // next sequence, so plain stores of the valid rows.
+      const bool store = tile_row0 + row < len;
+      __half* dst = args.out + static_cast<int64_t>(start + tile_row0 + row) * args.ld_out + h * kD;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        if (c >= 2 * halves) break;  // uniform over the CTA
+        const int ocol = col0 + c * 32;
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(o_addr + ocol, r);
+        tmem_ld_wait();
+        if (store) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            float o[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) o[e] = __uint_as_float(r[j + e]) * inv;
+            *reinterpret_cast<uint4*>(dst + ocol + j) =
+                make_uint4(pack_half2(o[0], o[1]), pack_half2(o[2], o[3]),
+                           pack_half2(o[4], o[5]), pack_half2(o[6], o[7]));
+          }
+        }
+      }
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
-    attention_kernel(const __grid_constant__ CUtensorMap map_qkv, const AttnArgs args) {
+    attention_kernel(const __grid_constant__ CUtensorMap map_qkv,
+                     const __grid_constant__ CUtensorMap map_out, const AttnArgs args) {
+  if (threadIdx.x == 0) OV_ATRACE(0);
   pdl_wait();
   pdl_trigger();
   int seq, tile, max_groups;
@@ -137,27 +348,40 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* k_s = q_s + 2 * kTile;       // [2 stages] x 32 KB
   uint8_t* v_s = k_s + 2 * kTile;       // [2 stages] x 32 KB
   uint64_t* bars = reinterpret_cast<uint64_t*>(v_s + 2 * kTile);
+  // K and V tiles have their own barriers: a K stage frees when its S
+  // MMAs are done, well before the P V that frees the V stage, so the
+  // next K tiles load ahead.
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // [2 groups]
-  uint64_t* p_full = bars + 7;    // [2 groups]
-  uint64_t* o_done = bars + 9;    // [2 groups]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+  uint64_t* k_full = bars + 1;    // [2 stages]
+  uint64_t* k_empty = bars + 3;   // [2]
+  uint64_t* v_full = bars + 5;    // [2]
+  uint64_t* v_empty = bars + 7;   // [2]
+  uint64_t* s_full = bars + 9;    // [2 groups, or 2 S regions of one tile]
+  uint64_t* p_full = bars + 11;   // [2]
+  uint64_t* o_done = bars + 13;   // [2 groups]
+  uint64_t* pv_done = bars + 15;  // one query tile: each P V complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  float* xmax = reinterpret_cast<float*>(bars + 18);  // [2 tiles][2 warpgroups][128 rows]
+  float* xsum = xmax + 512;                           // [2 warpgroups][128 rows]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
+      // One query tile: both softmax warpgroups arrive on p_full[0].
+      mbar_init(&p_full[i], groups == 1 ? 256 : 128);
       mbar_init(&o_done[i], 1);
     }
+    mbar_init(pv_done, 1);
     fence_mbar_init();
     tma_prefetch_map(&map_qkv);
+    tma_prefetch_map(&map_out);
   }
   if (warp == 9) {
     tmem_alloc(tmem_slot, 512);
@@ -167,35 +391,42 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) OV_ATRACE(1);
 
   if (warp == 8) {
-    if (lane == 0) {
-      const int qcol = h * kD;
-      const int kcol = (args.heads + kvh) * kD;
-      const int vcol = (args.heads + args.kv_heads + kvh) * kD;
-      mbar_arrive_expect_tx(q_full, groups * kTile);
-      for (int g = 0; g < groups; ++g) {
-        tma_load_2d(q_s + g * kTile, &map_qkv, q_full, qcol, start + q0 + g * kQ);
-        tma_load_2d(q_s + g * kTile + kHalfTile, &map_qkv, q_full, qcol + 64, start + q0 + g * kQ);
+    // Lane 0 loads Q and the K tiles, lane 1 the V tiles, each into a
+    // 2-deep ring; stage t & 1 is refilled once the MMAs reading it are done.
+    if (lane < 2) {
+      const bool keys = lane == 0;
+      const int col = keys ? (args.heads + kvh) * kD : (args.heads + args.kv_heads + kvh) * kD;
+      uint64_t* full = keys ? k_full : v_full;
+      uint64_t* empty = keys ? k_empty : v_empty;
+      uint8_t* ring = keys ? k_s : v_s;
+      if (keys) {
+        const int qcol = h * kD;
+        mbar_arrive_expect_tx(q_full, groups * kTile);
+        for (int g = 0; g < groups; ++g) {
+          tma_load_2d(q_s + g * kTile, &map_qkv, q_full, qcol, start + q0 + g * kQ);
+          tma_load_2d(q_s + g * kTile + kHalfTile, &map_qkv, q_full, qcol + 64,
+                      start + q0 + g * kQ);
+        }
       }
       int issued = 0;
       for (int t = 0; t < nt; ++t) {
         const int st = t & 1;
-        if (t >= 2 && !mbar_wait(&kv_empty[st], static_cast<uint32_t>((t >> 1) - 1) & 1u, args.err))
+        if (t >= 2 && !mbar_wait(&empty[st], static_cast<uint32_t>((t >> 1) - 1) & 1u, args.err))
           break;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * kTile);
+        mbar_arrive_expect_tx(&full[st], kTile);
         const int key0 = start + t * kKeys;
-        uint8_t* kd = k_s + st * kTile;
-        uint8_t* vd = v_s + st * kTile;
-        tma_load_2d(kd, &map_qkv, &kv_full[st], kcol, key0);
-        tma_load_2d(kd + kHalfTile, &map_qkv, &kv_full[st], kcol + 64, key0);
-        tma_load_2d(vd, &map_qkv, &kv_full[st], vcol, key0);
-        tma_load_2d(vd + kHalfTile, &map_qkv, &kv_full[st], vcol + 64, key0);
+        uint8_t* d = ring + st * kTile;
+        tma_load_2d(d, &map_qkv, &full[st], col, key0);
+        tma_load_2d(d + kHalfTile, &map_qkv, &full[st], col + 64, key0);
         ++issued;
       }
-      (void)mbar_wait(q_full, 0, args.err);
+      // Let this lane's copies land before the CTA can exit.
+      if (keys) (void)mbar_wait(q_full, 0, args.err);
       for (int t = issued > 2 ? issued - 2 : 0; t < issued; ++t)
-        (void)mbar_wait(&kv_full[t & 1], static_cast<uint32_t>(t >> 1) & 1u, args.err);
+        (void)mbar_wait(&full[t & 1], static_cast<uint32_t>(t >> 1) & 1u, args.err);
     }
   } else if (warp == 9) {
     if (lane == 0) {
@@ -225,15 +456,79 @@ __global__ void __launch_bounds__(kThreads, 1)
                       smem_desc_sw128(va + kk * 16 * 128, kHalfTile, 1024), idesc_o,
                       (t > 0 || kk > 0) ? 1u : 0u);
       };
-      bool ok = mbar_wait(q_full, 0, args.err) && mbar_wait(&kv_full[0], 0, args.err);
+      bool ok = mbar_wait(q_full, 0, args.err) && mbar_wait(&k_full[0], 0, args.err);
+      OV_ATRACE(2);
+      if (ok && groups == 1) {
+        // One query tile: S alternates between the two S/P regions, so
+        // S(t + 1) runs on the tensor core while the softmax turns S(t)
+        // into P(t).  S(j) reuses region j & 1 once P V(j - 2) was issued
+        // (in-order MMAs) and needs K(j); P V(j) needs P(j).  Whichever is
+        // ready goes first.
+        auto issue_s1 = [&](int t) {
+          const uint32_t ka = smem_u32(k_s + (t & 1) * kTile);
+          const uint32_t d = tmem + static_cast<uint32_t>((t & 1) * 256);
+#pragma unroll
+          for (int kk = 0; kk < kD / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * kHalfTile + (kk & 3) * 32;
+            umma_f16_ss(d, smem_desc_sw128(qa + off, 16, 1024),
+                        smem_desc_sw128(ka + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[t & 1]);
+          umma_commit(&k_empty[t & 1]);  // K(t) consumed
+        };
+        auto issue_pv1 = [&](int t) {
+          const uint32_t va = smem_u32(v_s + (t & 1) * kTile);
+          const uint32_t p = tmem + static_cast<uint32_t>((t & 1) * 256);
+          const uint32_t o = tmem + 128;
+#pragma unroll
+          for (int kk = 0; kk < kKeys / 16; ++kk)
+            umma_f16_ts(o, p + static_cast<uint32_t>(kk * 8),
+                        smem_desc_sw128(va + kk * 16 * 128, kHalfTile, 1024), idesc_o,
+                        (t > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(pv_done);
+          if (t == nt - 1) umma_commit(&o_done[0]);
+          umma_commit(&v_empty[t & 1]);  // V(t) consumed
+        };
+        tc_fence_after_sync();
+        issue_s1(0);
+        int next_s = 1, next_pv = 0;
+        uint64_t idle_since = 0;
+        while (next_pv < nt) {
+          bool progress = false;
+          if (next_s < nt && next_s <= next_pv + 1 &&
+              mbar_test_wait(&k_full[next_s & 1], static_cast<uint32_t>(next_s >> 1) & 1u)) {
+            tc_fence_after_sync();
+            issue_s1(next_s++);
+            progress = true;
+          }
+          if (next_pv < next_s &&
+              mbar_test_wait(&p_full[next_pv & 1], static_cast<uint32_t>(next_pv >> 1) & 1u) &&
+              mbar_test_wait(&v_full[next_pv & 1], static_cast<uint32_t>(next_pv >> 1) & 1u)) {
+            tc_fence_after_sync();
+            issue_pv1(next_pv++);
+            progress = true;
+          }
+          if (progress) {
+            idle_since = 0;
+          } else if (idle_since == 0) {
+            idle_since = global_timer_ns();
+          } else if (global_timer_ns() - idle_since > kWaitLimitNs) {
+            atomicOr(args.err, kErrWaitTimeout);
+            break;
+          }
+        }
+        ok = false;  // done: skip the two-tile schedule below
+      }
       if (ok) {
         tc_fence_after_sync();
         for (int g = 0; g < groups; ++g) issue_s(g, 0);
+        umma_commit(&k_empty[0]);
       }
       for (int t = 0; ok && t < nt; ++t) {
         const bool more = t + 1 < nt;
         for (int g = 0; g < groups; ++g) {
-          if (!mbar_wait(&p_full[g], static_cast<uint32_t>(t) & 1u, args.err)) {
+          if (!mbar_wait(&p_full[g], static_cast<uint32_t>(t) & 1u, args.err) ||
+              (g == 0 && !mbar_wait(&v_full[t & 1], static_cast<uint32_t>(t >> 1) & 1u, args.err))) {
             ok = false;
             break;
           }
@@ -243,7 +538,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             umma_commit(&o_done[g]);
             continue;
           }
-          if (g == 0 && !mbar_wait(&kv_full[(t + 1) & 1], static_cast<uint32_t>((t + 1) >> 1) & 1u,
+          if (g == 0 && !mbar_wait(&k_full[(t + 1) & 1], static_cast<uint32_t>((t + 1) >> 1) & 1u,
                                    args.err)) {
             ok = false;
             break;
@@ -251,127 +546,32 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after_sync();
           issue_s(g, t + 1);  // runs after this group's P V (in-order MMAs)
         }
-        umma_commit(&kv_empty[t & 1]);
+        if (!ok) break;
+        umma_commit(&v_empty[t & 1]);
+        if (more) umma_commit(&k_empty[(t + 1) & 1]);
       }
     }
   } else {
-    // Softmax groups: thread owns query row `row` of group g.
-    const int g = warp >> 2;
-    const int row = (warp & 3) * 32 + lane;
-    const bool active = g < groups;
-    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t s_addr = tmem + static_cast<uint32_t>(g * 256) + lane_off;
-    const uint32_t o_addr = s_addr + 128;
-    float m = -INFINITY, l = 0.0f;
-    bool ok = active;
-    for (int t = 0; ok && t < nt; ++t) {
-      // Warp-uniform outcome: the tensor-memory accesses below are
-      // warp-collective.
-      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&s_full[g], static_cast<uint32_t>(t) & 1u, args.err))) {
-        ok = false;
-        break;
-      }
-      tc_fence_after_sync();
-      const int valid = min(kKeys, len - t * kKeys);
-      // Pass 1: row maximum (two 32-column chunks in registers at a time;
-      // keys past the sequence end read as -inf).
-      float mt = -INFINITY;
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t ra[32], rb[32];
-        tmem_ld_32x32b_x32(s_addr + half * 64, ra);
-        tmem_ld_32x32b_x32(s_addr + half * 64 + 32, rb);
-        tmem_ld_wait();
-        if (valid < kKeys) {
-          mask_keys(ra, half * 64, valid);
-          mask_keys(rb, half * 64 + 32, valid);
-        }
-        mt = fmaxf(mt, fmaxf(max32(ra), max32(rb)));
-      }
-      mt *= args.scale_log2;
-      if (t == 0) {
-        m = mt;
-      } else {
-        // tcgen05.ld / st are warp-collective (.sync.aligned): the whole
-        // warp rescales when any of its rows needs it; rows whose maximum
-        // did not grow past the threshold keep theirs (alpha = 1).
-        const bool grow = mt > m + kRescaleThreshold;
-        if (__any_sync(0xFFFFFFFFu, grow)) {
-          // The previous P V of this group completed before S_t was written
-          // (one thread issues both, in order), so O is stable here.
-          const float m_new = grow ? mt : m;
-          const float alpha = ex2_approx(m - m_new);
-          l *= alpha;
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t r[32];
-            tmem_ld_32x32b_x32(o_addr + c * 32, r);
-            tmem_ld_wait();
-#pragma unroll
-            for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * alpha);
-            tmem_st_32x32b_x16(o_addr + c * 32,
-                               *reinterpret_cast<const uint32_t(*)[16]>(&r[0]));
-            tmem_st_32x32b_x16(o_addr + c * 32 + 16,
-                               *reinterpret_cast<const uint32_t(*)[16]>(&r[16]));
-          }
-          m = m_new;
-        }
-      }
-      // Pass 2: probabilities, written as half pairs over the consumed S
-      // columns (keys 32c..32c+31 -> columns 16c..16c+15).
-      float rowsum = 0.0f;
-      const float neg_m = -m;
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t ra[32], rb[32];
-        tmem_ld_32x32b_x32(s_addr + half * 64, ra);
-        tmem_ld_32x32b_x32(s_addr + half * 64 + 32, rb);
-        tmem_ld_wait();
-        if (valid < kKeys) {
-          mask_keys(ra, half * 64, valid);
-          mask_keys(rb, half * 64 + 32, valid);
-        }
-        uint32_t pa[16], pb[16];
-        rowsum += probs32(ra, args.scale_log2, neg_m, pa);
-        rowsum += probs32(rb, args.scale_log2, neg_m, pb);
-        tmem_st_32x32b_x16(s_addr + half * 32, pa);
-        tmem_st_32x32b_x16(s_addr + half * 32 + 16, pb);
-      }
-      l += rowsum;
-      tmem_st_wait();
-      tc_fence_before_sync();
-      mbar_arrive(&p_full[g]);
-    }
-    if (__all_sync(0xFFFFFFFFu, ok && mbar_wait(&o_done[g], 0, args.err))) {
-      tc_fence_after_sync();
-      const float inv = 1.0f / l;
-      const bool store = q0 + g * kQ + row < len;
-      __half* dst =
-          args.out + static_cast<int64_t>(start + q0 + g * kQ + row) * args.ld_out + h * kD;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(o_addr + c * 32, r);
-        tmem_ld_wait();
-        if (store) {
-#pragma unroll
-          for (int j = 0; j < 32; j += 8) {
-            float o[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) o[e] = __uint_as_float(r[j + e]) * inv;
-            *reinterpret_cast<uint4*>(dst + c * 32 + j) =
-                make_uint4(pack_half2(o[0], o[1]), pack_half2(o[2], o[3]),
-                           pack_half2(o[4], o[5]), pack_half2(o[6], o[7]));
-          }
-        }
-      }
-    }
+    if (groups == 1)
+      SoftmaxRole<true>(args, &map_out, tmem, s_full, p_full, o_done, pv_done, xmax, xsum, q_s,
+                        warp, lane, len, nt, q0, start, h);
+    else
+      SoftmaxRole<false>(args, &map_out, tmem, s_full, p_full, o_done, pv_done, xmax, xsum,
+                         q_s, warp, lane, len, nt, q0, start, h);
   }
   tc_fence_before_sync();
   __syncthreads();
   if (warp == 9) {
     tc_fence_after_sync();
     tmem_dealloc(tmem, 512);
+#ifdef OV_ATTN_TRACE
+    if (lane == 0) {
+      OV_ATRACE(6);
+      uint32_t smid;
+      asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+      g_attn_trace[(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z)) % 4096 * 8 + 7] = smid;
+    }
+#endif
   }
 }
 
@@ -384,9 +584,10 @@ void ConfigureAttentionKernel() {
 
 // items: device [n_items][2] (sequence, first 128-query tile | max groups
 // << 24); null to cover ceil(max_seqlen / 256) tile pairs of every sequence.
-void LaunchAttention(const CUtensorMap& map_qkv, const int32_t* cu_seqlens, int num_seqs,
-                     int max_seqlen, const int32_t* items, int n_items, int heads, int kv_heads,
-                     float scale, __half* out, int64_t ld_out, cudaStream_t stream) {
+void LaunchAttention(const CUtensorMap& map_qkv, const CUtensorMap& map_out,
+                     const int32_t* cu_seqlens, int num_seqs, int max_seqlen,
+                     const int32_t* items, int n_items, int heads, int kv_heads, float scale,
+                     __half* out, int64_t ld_out, cudaStream_t stream) {
   if (num_seqs == 0 || max_seqlen == 0) return;
   SetMaxDynamicSmem(reinterpret_cast<const void*>(attention_kernel),
                     static_cast<int>(kSmemBytes));
@@ -404,7 +605,14 @@ void LaunchAttention(const CUtensorMap& map_qkv, const int32_t* cu_seqlens, int 
                         : dim3(static_cast<unsigned>((max_seqlen + 2 * kQ - 1) / (2 * kQ)),
                                static_cast<unsigned>(num_seqs), static_cast<unsigned>(heads));
   Launch(attention_kernel, grid, dim3(kThreads), kSmemBytes, stream, "attention kernel launch",
-         map_qkv, a);
+         map_qkv, map_out, a);
+}
+
+void EncodeAttnOutMap(CUtensorMap* map, const uint16_t* out, int64_t ld_out, int64_t rows,
+                      int64_t width) {
+  EncodeTensorMap2D(map, out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, static_cast<uint64_t>(width),
+                    static_cast<uint64_t>(rows), static_cast<uint64_t>(ld_out) * 2, 64, 128,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 void EncodeQkvMap(CUtensorMap* map, const uint16_t* qkv, int64_t ld_qkv, int64_t rows,
@@ -418,6 +626,19 @@ void EncodeQkvMap(CUtensorMap* map, const uint16_t* qkv, int64_t ld_qkv, int64_t
 
 using namespace ovb;
 
+#ifdef OV_ATTN_TRACE
+extern "C" int ov_debug_attn_trace(unsigned long long* out, size_t count, int clear) {
+  if (clear) {
+    static unsigned long long zeros[4096 * 8];
+    return cudaMemcpyToSymbol(ovb::g_attn_trace, zeros, sizeof(zeros)) == cudaSuccess ? 0 : 2;
+  }
+  return cudaMemcpyFromSymbol(out, ovb::g_attn_trace, count * sizeof(unsigned long long)) ==
+                 cudaSuccess
+             ? 0
+             : 2;
+}
+#endif
+
 extern "C" int ov_attention_varlen(const uint16_t* qkv, size_t ld_qkv, size_t rows,
                                    const int32_t* cu_seqlens, size_t num_seqs,
                                    size_t max_seqlen, size_t heads, size_t kv_heads,
@@ -429,10 +650,13 @@ extern "C" int ov_attention_varlen(const uint16_t* qkv, size_t ld_qkv, size_t ro
     OV_REQUIRE(ld_qkv % 8 == 0 && ld_qkv >= (heads + 2 * kv_heads) * head_dim, "qkv stride");
     OV_REQUIRE(ld_out % 8 == 0 && ld_out >= heads * head_dim, "out stride");
     if (rows == 0 || num_seqs == 0) return;
-    CUtensorMap map;
+    OV_REQUIRE((reinterpret_cast<uintptr_t>(out) & 15u) == 0, "out must be 16-byte aligned");
+    CUtensorMap map, map_out;
     EncodeQkvMap(&map, qkv, static_cast<int64_t>(ld_qkv), static_cast<int64_t>(rows),
                  static_cast<int64_t>((heads + 2 * kv_heads) * head_dim));
-    LaunchAttention(map, cu_seqlens, static_cast<int>(num_seqs), static_cast<int>(max_seqlen),
+    EncodeAttnOutMap(&map_out, out, static_cast<int64_t>(ld_out), static_cast<int64_t>(rows),
+                     static_cast<int64_t>(heads * head_dim));
+    LaunchAttention(map, map_out, cu_seqlens, static_cast<int>(num_seqs), static_cast<int>(max_seqlen),
                     nullptr, 0, static_cast<int>(heads), static_cast<int>(kv_heads), scale,
                     reinterpret_cast<__half*>(out), static_cast<int64_t>(ld_out),
                     AsStream(stream));

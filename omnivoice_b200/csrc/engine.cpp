@@ -492,6 +492,7 @@ void Engine::BuildPlans() {
            static_cast<int>(2 * total_frames_), CV_, H_, OV_EPI_STORE_F32, nullptr, nullptr, 0,
            sms_);
   EncodeQkvMap(&qkv_map_, qkv_.get(), QKVW_, R_, QKVW_);
+  EncodeAttnOutMap(&attn_out_map_, attn_.get(), QH_, R_, QH_);
 }
 
 void Engine::EnqueueForward(cudaStream_t s, Marker* m) {
@@ -527,7 +528,7 @@ void Engine::EnqueueForward(cudaStream_t s, Marker* m) {
     mark(kGemmQkv, 2.0 * R * H * QKVW_, 0.0);
     LaunchGemm(p.qkv, s);
     mark(kAttention, attn_flops, 0.0);
-    LaunchAttention(qkv_map_, cu_seqlens_.get(), static_cast<int>(n_seqs_),
+    LaunchAttention(qkv_map_, attn_out_map_, cu_seqlens_.get(), static_cast<int>(n_seqs_),
                     static_cast<int>(max_seqlen_), attn_items_.get(),
                     static_cast<int>(n_items_), static_cast<int>(cfg_.heads),
                     static_cast<int>(cfg_.kv_heads), scale,

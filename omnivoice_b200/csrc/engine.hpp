@@ -128,6 +128,7 @@ class Engine {
   std::vector<LayerPlans> plans_;
   GemmPlan head_plan_;
   CUtensorMap qkv_map_;
+  CUtensorMap attn_out_map_;
   cudaGraph_t graph_ = nullptr;
   cudaGraphExec_t graph_exec_ = nullptr;
   size_t kernels_per_step_ = 0;

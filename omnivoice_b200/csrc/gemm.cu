@@ -721,7 +721,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (c.ep == 0) OV_TRACE(6);
       }
     }
-    if (c.gep == 0) bulk_wait_group<0>();  // each group leader's stores
+    // Each group leader's stores have read their staging tiles before the
+    // CTA's shared memory goes away; the writes complete with the grid.
+    if (c.gep == 0) bulk_wait_group_read<0>();
 #ifdef OV_GEMM_TRACE
     if (c.ep == 0) {
       OV_TRACE(7);

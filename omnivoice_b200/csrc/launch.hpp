@@ -77,12 +77,16 @@ void LaunchRmsNorm(const float* input, const int32_t* indices, size_t rows, cons
 
 void EncodeQkvMap(CUtensorMap* map, const uint16_t* qkv, int64_t ld_qkv, int64_t rows,
                   int64_t width);
+// Attention output [rows][width] fp16 as 128B-swizzled [128][64] boxes.
+void EncodeAttnOutMap(CUtensorMap* map, const uint16_t* out, int64_t ld_out, int64_t rows,
+                      int64_t width);
 // items: device [n_items][2] (sequence, pair of 128-query tiles), longest
 // sequences first; null covers ceil(max_seqlen / 256) pairs of every
 // sequence (CTAs past a sequence's end exit at once).
-void LaunchAttention(const CUtensorMap& map_qkv, const int32_t* cu_seqlens, int num_seqs,
-                     int max_seqlen, const int32_t* items, int n_items, int heads, int kv_heads,
-                     float scale, __half* out, int64_t ld_out, cudaStream_t stream);
+void LaunchAttention(const CUtensorMap& map_qkv, const CUtensorMap& map_out,
+                     const int32_t* cu_seqlens, int num_seqs, int max_seqlen,
+                     const int32_t* items, int n_items, int heads, int kv_heads, float scale,
+                     __half* out, int64_t ld_out, cudaStream_t stream);
 
 void LaunchScore(const float* logits, int64_t ld, int total_frames, int codebooks, int vocab,
                  uint32_t mask_id, float guidance, const UttDesc* utts, const int32_t* frame_utt,
