@@ -303,14 +303,19 @@ __device__ __forceinline__ void EpilogueUnit(const GemmArgs& a, const CUtensorMa
       const uint32_t th = tacc + hh * 128;
       if (slot < a.heads + a.kv_heads) {
         const float* w = norm_w + (slot < a.heads ? 0 : 128);
+        // RMS of the head: four 16-column loads in flight per wait.
         float ss = 0.0f;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          uint32_t r[16];
-          tmem_ld_32x32b_x16(th + q * 16, r);
+        for (int q4 = 0; q4 < 8; q4 += 4) {
+          uint32_t r[4][16];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) tmem_ld_32x32b_x16(th + (q4 + q) * 16, r[q]);
           tmem_ld_wait();
 #pragma unroll
-          for (int j = 0; j < 16; ++j) ss = fmaf(__uint_as_float(r[j]), __uint_as_float(r[j]), ss);
+          for (int q = 0; q < 4; ++q)
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              ss = fmaf(__uint_as_float(r[q][j]), __uint_as_float(r[q][j]), ss);
         }
         const float scale = 1.0f / sqrtf(ss / 128.0f + a.epsilon);
         uint32_t lo[16], hi[16];
