@@ -52,10 +52,12 @@ constexpr int kRingBytes = 196608;
 constexpr uint32_t kStageTile = 128 * 128;  // one staging tile: 128 rows x 128 bytes
 constexpr int kGroupM = 8;                  // rasterisation group of m tiles
 
-template <int BN, int EPI>
+// PAIR: a CTA pair runs 256-row tiles with cta_group::2 MMAs; each CTA
+// loads its 128 rows of A and half (BN / 2 rows) of the B tile.
+template <int BN, int EPI, bool PAIR = false>
 struct TileConfig {
   static constexpr uint32_t kABytes = kBM * kBK * 2;
-  static constexpr uint32_t kBBytes = BN * kBK * 2;
+  static constexpr uint32_t kBBytes = (PAIR ? BN / 2 : BN) * kBK * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   static constexpr int kStages = kRingBytes / kStageBytes;
   static constexpr uint32_t kNormFloats = EPI == OV_EPI_QKNORM_ROPE_F16 ? 256 : 0;
@@ -476,13 +478,17 @@ __device__ unsigned long long g_gemm_trace[1024 * 16];
   } while (0)
 #endif
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                 const __grid_constant__ CUtensorMap map_y, const GemmArgs args) {
-  using Cfg = TileConfig<BN, EPI>;
+  using Cfg = TileConfig<BN, EPI, PAIR>;
   constexpr int kStages = Cfg::kStages;
-  constexpr bool kClusterSplit = EPI == OV_EPI_ACCUM_F32 || EPI == OV_EPI_STORE_F32;
+  constexpr bool kClusterSplit = !PAIR && (EPI == OV_EPI_ACCUM_F32 || EPI == OV_EPI_STORE_F32);
+  // PAIR: units are 256-row tiles walked by CTA pairs; rank 0 issues the MMAs.
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const int unit0 = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int ustep = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -509,7 +515,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 256);
+      // PAIR: one arrival from each CTA's epilogue (on rank 0's barrier).
+      mbar_init(&tempty[b], PAIR ? 2 : 256);
     }
     mbar_init(inbox_bar, 1);
     fence_mbar_init();
@@ -518,8 +525,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_map(&map_y);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 2 * BN);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, 2 * BN);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, 2 * BN);
+      tmem_relinquish();
+    }
   }
   if constexpr (EPI == OV_EPI_QKNORM_ROPE_F16) {
     if (warp >= 2) {
@@ -528,7 +540,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   tc_fence_before_sync();
-  __syncthreads();
+  if constexpr (PAIR)
+    cluster_sync();  // both CTAs' barriers exist before any cross-CTA signal
+  else
+    __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem = *tmem_slot;
   if (threadIdx.x == 0) OV_TRACE(1);
@@ -541,17 +556,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       // The weights do not depend on the previous kernel: start the weight
       // tiles of the first ring slots before waiting for it.
+      //
+      // PAIR: each CTA loads its A rows (256-row tile m: rows 256 m + 128
+      // rank ..) and its half of the B rows into its own ring; all bytes
+      // complete on rank 0's full barrier, which rank 0 arms for both.
+      const uint32_t stage_tx = PAIR ? 2 * Cfg::kStageBytes : Cfg::kStageBytes;
+      const bool arm = !PAIR || rank == 0;
+      const int b_rows = PAIR ? BN / 2 : BN;
+      auto bar_of = [&](int st) -> uint32_t {
+        return PAIR ? mapa_shared(smem_u32(&full[st]), 0) : smem_u32(&full[st]);
+      };
+      auto load = [&](void* dst, const CUtensorMap* map, int st, int x, int y) {
+        if constexpr (PAIR)
+          tma_load_2d_pair(dst, map, bar_of(st), x, y);
+        else
+          tma_load_2d(dst, map, &full[st], x, y);
+      };
       uint32_t pre = 0;
-      if (static_cast<int>(blockIdx.x) < args.units) {
+      if (unit0 < args.units) {
         int m_tile, n_tile, split;
-        UnitCoords(args, blockIdx.x, m_tile, n_tile, split);
+        UnitCoords(args, unit0, m_tile, n_tile, split);
         const int kb0 = split * args.kblocks / args.splits;
         const int kb1 = (split + 1) * args.kblocks / args.splits;
         pre = static_cast<uint32_t>(min(kStages, kb1 - kb0));
         for (uint32_t i = 0; i < pre; ++i) {
-          mbar_arrive_expect_tx(&full[i], Cfg::kStageBytes);
-          tma_load_2d(sb + i * Cfg::kBBytes, &map_b, &full[i], (kb0 + static_cast<int>(i)) * kBK,
-                      args.b_row_offset + n_tile * BN);
+          if (arm) mbar_arrive_expect_tx(&full[i], stage_tx);
+          load(sb + i * Cfg::kBBytes, &map_b, static_cast<int>(i),
+               (kb0 + static_cast<int>(i)) * kBK,
+               args.b_row_offset + n_tile * BN + static_cast<int>(rank) * b_rows);
         }
       }
       pdl_wait();
@@ -559,16 +591,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       OV_TRACE(2);
       uint32_t k_iter = 0;
       bool ok = true;
-      for (int u = blockIdx.x; ok && u < args.units; u += gridDim.x) {
+      for (int u = unit0; ok && u < args.units; u += ustep) {
         int m_tile, n_tile, split;
         UnitCoords(args, u, m_tile, n_tile, split);
+        const int a_row = (PAIR ? 2 * m_tile + static_cast<int>(rank) : m_tile) * kBM;
         const int kb0 = split * args.kblocks / args.splits;
         const int kb1 = (split + 1) * args.kblocks / args.splits;
         for (int kb = kb0; kb < kb1; ++kb, ++k_iter) {
           const int s = static_cast<int>(k_iter % kStages);
           const uint32_t phase = (k_iter / kStages) & 1u;
           if (k_iter < pre) {  // weight tile already on its way
-            tma_load_2d(sa + s * Cfg::kABytes, &map_a, &full[s], kb * kBK, m_tile * kBM);
+            load(sa + s * Cfg::kABytes, &map_a, s, kb * kBK, a_row);
             continue;
           }
           if (k_iter >= static_cast<uint32_t>(kStages) &&
@@ -576,17 +609,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
-          tma_load_2d(sa + s * Cfg::kABytes, &map_a, &full[s], kb * kBK, m_tile * kBM);
-          tma_load_2d(sb + s * Cfg::kBBytes, &map_b, &full[s], kb * kBK,
-                      args.b_row_offset + n_tile * BN);
+          if (arm) mbar_arrive_expect_tx(&full[s], stage_tx);
+          load(sa + s * Cfg::kABytes, &map_a, s, kb * kBK, a_row);
+          load(sb + s * Cfg::kBBytes, &map_b, s, kb * kBK,
+               args.b_row_offset + n_tile * BN + static_cast<int>(rank) * b_rows);
         }
       }
       OV_TRACE(10);
-      // Let the copies this thread started land before the CTA can exit.
-      const uint32_t first = k_iter > static_cast<uint32_t>(kStages) ? k_iter - kStages : 0u;
-      for (uint32_t i = first; i < k_iter; ++i)
-        (void)mbar_wait(&full[i % kStages], (i / kStages) & 1u, args.err);
+      // Let the copies this thread started land before the CTA can exit
+      // (PAIR rank 1: its copies land on rank 0's barriers, which rank 0's
+      // MMAs consume before this CTA's accumulators are complete).
+      if (arm) {
+        const uint32_t first = k_iter > static_cast<uint32_t>(kStages) ? k_iter - kStages : 0u;
+        for (uint32_t i = first; i < k_iter; ++i)
+          (void)mbar_wait(&full[i % kStages], (i / kStages) & 1u, args.err);
+      }
     }
     if (kClusterSplit && args.cluster) {  // the two barriers of the split-K reduction
       __syncwarp();
@@ -594,12 +631,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       cluster_sync();
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16_f32(kBM, BN);
+    if (lane == 0 && rank == 0) {  // PAIR: rank 0 issues for both CTAs
+      constexpr uint32_t idesc = idesc_f16_f32(PAIR ? 2 * kBM : kBM, BN);
       uint32_t k_iter = 0;
       int acc_iter = 0;
       bool ok = true;
-      for (int u = blockIdx.x; ok && u < args.units; u += gridDim.x, ++acc_iter) {
+      for (int u = unit0; ok && u < args.units; u += ustep, ++acc_iter) {
         int m_tile, n_tile, split;
         UnitCoords(args, u, m_tile, n_tile, split);
         const int kb0 = split * args.kblocks / args.splits;
@@ -624,13 +661,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t a0 = smem_u32(sa + s * Cfg::kABytes);
           const uint32_t b0 = smem_u32(sb + s * Cfg::kBBytes);
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k)
-            umma_f16_ss(d, smem_desc_sw128(a0 + k * 32, 16, 1024),
-                        smem_desc_sw128(b0 + k * 32, 16, 1024), idesc,
-                        (kb > kb0 || k > 0) ? 1u : 0u);
-          umma_commit(&empty[s]);
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t ad = smem_desc_sw128(a0 + k * 32, 16, 1024);
+            const uint64_t bd = smem_desc_sw128(b0 + k * 32, 16, 1024);
+            const uint32_t acc = (kb > kb0 || k > 0) ? 1u : 0u;
+            if constexpr (PAIR)
+              umma_f16_ss_pair(d, ad, bd, idesc, acc);
+            else
+              umma_f16_ss(d, ad, bd, idesc, acc);
+          }
+          if constexpr (PAIR)
+            umma_commit_pair(&empty[s], 0x3);  // both CTAs' slots are free
+          else
+            umma_commit(&empty[s]);
         }
-        umma_commit(&tfull[buf]);
+        if constexpr (PAIR)
+          umma_commit_pair(&tfull[buf], 0x3);
+        else
+          umma_commit(&tfull[buf]);
         if (acc_iter == 0) OV_TRACE(4);
       }
       OV_TRACE(11);
@@ -652,9 +700,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;  // tensor-memory lanes 32*quarter .. +31
     c.row = quarter * 32 + lane;
     int acc_iter = 0;
-    for (int u = blockIdx.x; u < args.units; u += gridDim.x, ++acc_iter) {
+    for (int u = unit0; u < args.units; u += ustep, ++acc_iter) {
       int m_tile, n_tile, split;
       UnitCoords(args, u, m_tile, n_tile, split);
+      if constexpr (PAIR) m_tile = 2 * m_tile + static_cast<int>(rank);  // this CTA's 128 rows
       const int buf = acc_iter & 1;
       RopeRow rope;
       LoadRopeRow<EPI>(args, m_tile, c.row, c.group, rope);
@@ -678,10 +727,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t tacc =
           tmem + static_cast<uint32_t>(buf * BN) + (static_cast<uint32_t>(quarter * 32) << 16);
       // This CTA's last unit: its loads are all consumed and its MMAs done.
-      c.ring = u + static_cast<int>(gridDim.x) >= args.units ? smem : nullptr;
+      c.ring = u + ustep >= args.units ? smem : nullptr;
       EpilogueUnit<BN, EPI>(args, &map_y, c, tacc, m_tile, n_tile, norm_w, rope);
       tc_fence_before_sync();
-      mbar_arrive(&tempty[buf]);
+      if constexpr (PAIR) {
+        // Both CTAs' accumulators are read: one arrival per CTA on rank 0.
+        named_barrier(kEpiBarrier, 256);
+        if (c.ep == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[buf]), 0));
+      } else {
+        mbar_arrive(&tempty[buf]);
+      }
       if (EPI == OV_EPI_ACCUM_F32 && args.splits > 1) {
         if (c.gep == 0) {  // both group leaders: their adds are complete
           bulk_wait_group<0>();
@@ -740,30 +795,46 @@ __global__ void __launch_bounds__(kThreads, 1)
 #endif
   }
   tc_fence_before_sync();
-  __syncthreads();
+  if constexpr (PAIR)
+    cluster_sync();  // no CTA leaves while its peer may still signal it
+  else
+    __syncthreads();
   if (threadIdx.x == 0) OV_TRACE(8);
   if (warp == 1) {
     tc_fence_after_sync();
-    tmem_dealloc(tmem, 2 * BN);
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem, 2 * BN);
+    else
+      tmem_dealloc(tmem, 2 * BN);
   }
 }
 
-// Every compiled (tile width, epilogue) pair.
-#define OV_GEMM_INSTANCES(X)           \
-  X(64, OV_EPI_STORE_F32)              \
-  X(128, OV_EPI_STORE_F32)             \
-  X(256, OV_EPI_STORE_F32)             \
-  X(64, OV_EPI_ACCUM_F32)              \
-  X(128, OV_EPI_ACCUM_F32)             \
-  X(256, OV_EPI_ACCUM_F32)             \
-  X(128, OV_EPI_SWIGLU_F16)            \
-  X(256, OV_EPI_SWIGLU_F16)            \
-  X(128, OV_EPI_QKNORM_ROPE_F16)       \
-  X(256, OV_EPI_QKNORM_ROPE_F16)
+// Every compiled (tile width, epilogue, CTA pair) instance.
+#define OV_GEMM_INSTANCES(X)                 \
+  X(64, OV_EPI_STORE_F32, false)             \
+  X(128, OV_EPI_STORE_F32, false)            \
+  X(256, OV_EPI_STORE_F32, false)            \
+  X(64, OV_EPI_ACCUM_F32, false)             \
+  X(128, OV_EPI_ACCUM_F32, false)            \
+  X(256, OV_EPI_ACCUM_F32, false)            \
+  X(128, OV_EPI_SWIGLU_F16, false)           \
+  X(256, OV_EPI_SWIGLU_F16, false)           \
+  X(128, OV_EPI_QKNORM_ROPE_F16, false)      \
+  X(256, OV_EPI_QKNORM_ROPE_F16, false)      \
+  X(256, OV_EPI_STORE_F32, true)             \
+  X(256, OV_EPI_ACCUM_F32, true)             \
+  X(256, OV_EPI_SWIGLU_F16, true)            \
+  X(256, OV_EPI_QKNORM_ROPE_F16, true)
 
-template <int BN, int EPI>
+// Switch key of an instance.
+constexpr int InstanceKey(int bn, int epilogue, bool pair) {
+  return epilogue * 1000 + bn + (pair ? 100000 : 0);
+}
+
+template <int BN, int EPI, bool PAIR>
 void LaunchTyped(const GemmPlan& p, cudaStream_t stream) {
-  LaunchEx(gemm_kernel<BN, EPI>, p.grid, dim3(kThreads), TileConfig<BN, EPI>::kSmemBytes, stream,
+  LaunchEx(gemm_kernel<BN, EPI, PAIR>, p.grid, dim3(kThreads),
+           TileConfig<BN, EPI, PAIR>::kSmemBytes, stream,
            "gemm kernel launch", p.cluster_x, p.map_a, p.map_b, p.map_y, p.args);
 }
 
@@ -789,6 +860,16 @@ bool ValidShape(int bn, int splits, bool cluster, int N, int K, int epilogue) {
   }
 }
 
+// Epilogues and widths the CTA-pair kernel is built for.
+bool ValidPairShape(int bn, int N, int epilogue) {
+  if (bn != 256) return false;
+  switch (epilogue) {
+    case OV_EPI_SWIGLU_F16:
+    case OV_EPI_QKNORM_ROPE_F16: return N % 256 == 0;
+    default: return true;
+  }
+}
+
 // CTAs of one GEMM kernel that can be resident at once in clusters of
 // 1, 2, 4 and 8 (index log2), measured per device by ConfigureGemmKernels;
 // 0 until then (the chooser then assumes one cluster per 8 SMs).
@@ -810,9 +891,12 @@ GemmShapeChoice ChooseGemmShape(int M, int N, int K, int epilogue, bool have_wor
     char sep = 'x';
     if (std::sscanf(env, "%d%c%d", &bn, &sep, &splits) >= 1) {
       const bool cluster = sep == 'c';
-      if (ValidShape(bn, splits, cluster, N, K, epilogue) &&
-          (splits == 1 || cluster || have_workspace))
+      if (sep == 'p') {
+        if (ValidPairShape(bn, N, epilogue)) return {bn, 1, false, true};
+      } else if (ValidShape(bn, splits, cluster, N, K, epilogue) &&
+                 (splits == 1 || cluster || have_workspace)) {
         return {bn, splits, cluster && splits > 1};
+      }
     }
   }
   // Cost in units of one 64-deep k block of one CTA (about 0.3 us on
@@ -846,6 +930,16 @@ GemmShapeChoice ChooseGemmShape(int M, int N, int K, int epilogue, bool have_wor
         }
       }
     }
+  }
+  // CTA pairs: 256 x 256 tiles; a k block of a CTA moves 32 KB instead of
+  // the 48 KB of a 128 x 256 tile, so a long k loop runs at the MMA rate;
+  // the pair's start-up costs about one k block more (measured: pairs win
+  // from two rounds of tiles on, single CTAs on one round).
+  if (ValidPairShape(256, N, epilogue)) {
+    const double units = static_cast<double>(((M + 2 * kBM - 1) / (2 * kBM)) * ((N + 255) / 256));
+    const double pairs = ClusterCapacity(2, sms) / 2;
+    const double cost = std::ceil(units / pairs) * kblocks * 0.85 + kFill + 3.0;
+    if (cost < best_cost - 1e-9) best = {256, 1, false, true};
   }
   return best;
 }
@@ -888,6 +982,7 @@ void PlanGemm(GemmPlan* plan, const uint16_t* x, int64_t ldx, const uint16_t* w,
   }
   plan->epilogue = epilogue;
   plan->bn = choice.bn;
+  plan->pair = choice.pair;
   GemmArgs& a = plan->args;
   a = GemmArgs{};
   a.M = M;
@@ -896,7 +991,7 @@ void PlanGemm(GemmPlan* plan, const uint16_t* x, int64_t ldx, const uint16_t* w,
   a.kblocks = K / kBK;
   a.splits = choice.splits;
   a.b_row_offset = b_row_offset;
-  a.num_m = (M + kBM - 1) / kBM;
+  a.num_m = (M + kBM * (choice.pair ? 2 : 1) - 1) / (kBM * (choice.pair ? 2 : 1));
   a.num_n = (N + choice.bn - 1) / choice.bn;
   a.units = a.num_m * a.num_n * a.splits;
   a.out_cols = out_cols;
@@ -920,7 +1015,8 @@ void PlanGemm(GemmPlan* plan, const uint16_t* x, int64_t ldx, const uint16_t* w,
                     CU_TENSOR_MAP_SWIZZLE_128B);
   EncodeTensorMap2D(&plan->map_b, w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, static_cast<uint64_t>(K),
                     static_cast<uint64_t>(w_rows), static_cast<uint64_t>(K) * 2, kBK,
-                    static_cast<uint32_t>(choice.bn), CU_TENSOR_MAP_SWIZZLE_128B);
+                    static_cast<uint32_t>(choice.pair ? choice.bn / 2 : choice.bn),
+                    CU_TENSOR_MAP_SWIZZLE_128B);
   // y: 128-byte row pieces (32 floats or 64 halves) x 128 rows per box.
   if (half_out)
     EncodeTensorMap2D(&plan->map_y, y, CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
@@ -936,10 +1032,17 @@ void PlanGemm(GemmPlan* plan, const uint16_t* x, int64_t ldx, const uint16_t* w,
   int grid = std::min(a.units, sms);
   if (a.splits > 1) grid = std::max(a.splits, grid / a.splits * a.splits);
   if (a.cluster) grid = a.units;
+  if (choice.pair) {
+    // Persistent CTA pairs, one pair per two SMs that a 2-cluster can hold.
+    grid = 2 * std::max(1, std::min(a.units, ClusterCapacity(2, sms) / 2));
+    plan->cluster_x = 2;
+  }
   plan->grid = dim3(static_cast<unsigned>(grid), 1, 1);
-  switch (epilogue * 1000 + choice.bn) {
-#define OV_SMEM_CASE(BN, EPI) \
-  case EPI * 1000 + BN: plan->smem_bytes = TileConfig<BN, EPI>::kSmemBytes; break;
+  switch (InstanceKey(choice.bn, epilogue, choice.pair)) {
+#define OV_SMEM_CASE(BN, EPI, PAIR)   \
+  case InstanceKey(BN, EPI, PAIR): \
+    plan->smem_bytes = TileConfig<BN, EPI, PAIR>::kSmemBytes; \
+    break;
     OV_GEMM_INSTANCES(OV_SMEM_CASE)
 #undef OV_SMEM_CASE
     default: throw Error(OV_ERR_UNSUPPORTED, "no GEMM kernel for this epilogue / tile");
@@ -947,9 +1050,9 @@ void PlanGemm(GemmPlan* plan, const uint16_t* x, int64_t ldx, const uint16_t* w,
 }
 
 void ConfigureGemmKernels() {
-#define OV_CONFIGURE(BN, EPI)                                                   \
-  SetMaxDynamicSmem(reinterpret_cast<const void*>(gemm_kernel<BN, EPI>),        \
-                    static_cast<int>(TileConfig<BN, EPI>::kSmemBytes));
+#define OV_CONFIGURE(BN, EPI, PAIR)                                             \
+  SetMaxDynamicSmem(reinterpret_cast<const void*>(gemm_kernel<BN, EPI, PAIR>),  \
+                    static_cast<int>(TileConfig<BN, EPI, PAIR>::kSmemBytes));
   OV_GEMM_INSTANCES(OV_CONFIGURE)
 #undef OV_CONFIGURE
   int dev = 0;
@@ -970,7 +1073,7 @@ void ConfigureGemmKernels() {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int clusters = 0;
-    if (cudaOccupancyMaxActiveClusters(&clusters, gemm_kernel<256, OV_EPI_ACCUM_F32>, &cfg) !=
+    if (cudaOccupancyMaxActiveClusters(&clusters, gemm_kernel<256, OV_EPI_ACCUM_F32, false>, &cfg) !=
         cudaSuccess) {
       ClearError();
       clusters = 0;
@@ -980,12 +1083,12 @@ void ConfigureGemmKernels() {
 }
 
 void LaunchGemm(const GemmPlan& p, cudaStream_t stream) {
-  switch (p.epilogue * 1000 + p.bn) {
-#define OV_LAUNCH_CASE(BN, EPI)                                                 \
-  case EPI * 1000 + BN:                                                         \
-    SetMaxDynamicSmem(reinterpret_cast<const void*>(gemm_kernel<BN, EPI>),      \
-                      static_cast<int>(TileConfig<BN, EPI>::kSmemBytes));       \
-    LaunchTyped<BN, EPI>(p, stream);                                            \
+  switch (InstanceKey(p.bn, p.epilogue, p.pair)) {
+#define OV_LAUNCH_CASE(BN, EPI, PAIR)                                             \
+  case InstanceKey(BN, EPI, PAIR):                                                \
+    SetMaxDynamicSmem(reinterpret_cast<const void*>(gemm_kernel<BN, EPI, PAIR>),  \
+                      static_cast<int>(TileConfig<BN, EPI, PAIR>::kSmemBytes));   \
+    LaunchTyped<BN, EPI, PAIR>(p, stream);                                        \
     break;
     OV_GEMM_INSTANCES(OV_LAUNCH_CASE)
 #undef OV_LAUNCH_CASE
@@ -1031,9 +1134,10 @@ void NoAllocSetup(uint8_t** scratch, uint32_t** status) {
     Check(cudaGetSymbolAddress(&tp, g_noalloc_status), "cudaGetSymbolAddress(status)");
     Check(cudaMemset(sp, 0, kNoAllocScratchBytes), "clear split-K counters");
     Check(cudaMemset(tp, 0, sizeof(uint32_t) * 64), "clear status word");
-#define OV_SET_DIRECT(BN, EPI)                                                                 \
-  Check(cudaFuncSetAttribute(gemm_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                             static_cast<int>(TileConfig<BN, EPI>::kSmemBytes)),               \
+#define OV_SET_DIRECT(BN, EPI, PAIR)                                                   \
+  Check(cudaFuncSetAttribute(gemm_kernel<BN, EPI, PAIR>,                               \
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,              \
+                             static_cast<int>(TileConfig<BN, EPI, PAIR>::kSmemBytes)), \
         "cudaFuncSetAttribute(max dynamic shared memory)");
     OV_GEMM_INSTANCES(OV_SET_DIRECT)
 #undef OV_SET_DIRECT
@@ -1109,9 +1213,9 @@ int ov_gemm_f16_noalloc(const uint16_t* x, size_t ldx, const uint16_t* w, void* 
     PlanGemm(&plan, x, static_cast<int64_t>(ldx), w, static_cast<int64_t>(out), 0, y,
              static_cast<int64_t>(ldy), static_cast<int>(rows), static_cast<int>(out),
              static_cast<int>(in), epilogue, args, scratch, kNoAllocScratchBytes, sms, status);
-    switch (plan.epilogue * 1000 + plan.bn) {
-#define OV_DIRECT_CASE(BN, EPI) \
-  case EPI * 1000 + BN: LaunchTyped<BN, EPI>(plan, AsStream(stream)); break;
+    switch (InstanceKey(plan.bn, plan.epilogue, plan.pair)) {
+#define OV_DIRECT_CASE(BN, EPI, PAIR) \
+  case InstanceKey(BN, EPI, PAIR): LaunchTyped<BN, EPI, PAIR>(plan, AsStream(stream)); break;
       OV_GEMM_INSTANCES(OV_DIRECT_CASE)
 #undef OV_DIRECT_CASE
       default: throw Error(OV_ERR_UNSUPPORTED, "no GEMM kernel for this epilogue / tile");

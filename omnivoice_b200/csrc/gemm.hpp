@@ -54,16 +54,19 @@ struct GemmPlan {
   int epilogue = OV_EPI_STORE_F32;
   size_t smem_bytes = 0;
   unsigned cluster_x = 1;  // CTAs per thread-block cluster
+  bool pair = false;       // 256-row tiles on CTA pairs (cta_group::2)
 };
 
 struct GemmShapeChoice {
   int bn;
   int splits;
   bool cluster = false;  // splits reduced inside a thread-block cluster
+  bool pair = false;     // 256-row tiles on CTA pairs (cta_group::2 MMAs)
 };
 
 // Tile width and split-K factor for a product of this shape on `sms` SMs.
-// OV_GEMM_TILE=<bn>x<splits> in the environment overrides the choice
+// OV_GEMM_TILE=<bn>x<splits> (serialised split-K), <bn>c<splits> (cluster
+// split-K) or <bn>p1 (CTA pairs) in the environment overrides the choice
 // (tuning aid; ignored when the override is not valid for the product).
 GemmShapeChoice ChooseGemmShape(int M, int N, int K, int epilogue, bool have_workspace, int sms);
 // Workspace bytes a plan with this shape needs for split-K (0 if none).

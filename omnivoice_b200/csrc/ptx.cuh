@@ -370,6 +370,71 @@ __device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst, uint32_t src, ui
       : "memory");
 }
 
+// --------------------------------------------------- CTA pairs (cta_group::2)
+//
+// A CTA pair (a cluster of two) runs one tcgen05.mma of M = 256: each CTA
+// holds 128 rows of A and half of B's rows in its shared memory (same
+// offsets), and receives its 128 rows of D in its own tensor memory.  The
+// MMAs are issued by rank 0 only.
+
+// Tensor-memory allocation for both CTAs of the pair; one warp of each CTA
+// (the same warp index) executes it with the same `slot` offset.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* slot, uint32_t columns) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(slot)),
+               "r"(columns)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t columns) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(columns)
+               : "memory");
+}
+
+// D[tmem] (+)= A * B over the pair (M = 256), issued by rank 0.
+__device__ __forceinline__ void umma_f16_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                 uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives once on the mbarrier at `bar`'s offset in every CTA of `cta_mask`
+// when the pair MMAs issued so far by this thread have completed.
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(smem_u32(bar)),
+      "h"(cta_mask)
+      : "memory");
+}
+
+// 2-D tiled load into this CTA's shared memory whose transaction bytes
+// complete on `bar_cluster` (a shared::cluster address, rank 0's barrier).
+// No multicast: each CTA loads its own tiles.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map,
+                                                 uint32_t bar_cluster, int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+
+// Arrive (release, cluster scope) on an mbarrier given by its shared::cluster
+// address, possibly in the peer CTA.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster)
+               : "memory");
+}
+
 // ------------------------------------------- programmatic dependent launch
 
 // Waits until the grids this one depends on (launched before it in the

@@ -214,12 +214,13 @@ def test_gemm_residual_split_k_is_deterministic(M, K):
 
 
 @pytest.mark.parametrize("tile", ["64x1", "128x1", "256x1", "64x3", "128x2", "256x4",
-                                  "64c2", "128c4", "256c2", "256c8"])
+                                  "64c2", "128c4", "256c2", "256c8", "256p1"])
 @pytest.mark.parametrize("epi", [N.OV_EPI_STORE_F32, N.OV_EPI_ACCUM_F32])
 def test_gemm_every_tile_shape(monkeypatch, tile, epi):
     """Each compiled tile width, serialised split-K factor (<bn>x<splits>,
-    residual add only) and cluster split-K factor (<bn>c<splits>), forced
-    through OV_GEMM_TILE, against float64 on ragged M and N."""
+    residual add only), cluster split-K factor (<bn>c<splits>) and the
+    CTA-pair kernel (256p1), forced through OV_GEMM_TILE, against float64
+    on ragged M and N."""
     if epi == N.OV_EPI_STORE_F32 and "x" in tile and not tile.endswith("x1"):
         pytest.skip("serialised split-K applies to the residual epilogue only")
     monkeypatch.setenv("OV_GEMM_TILE", tile)
@@ -243,7 +244,10 @@ def test_gemm_every_tile_shape(monkeypatch, tile, epi):
     assert torch.equal(outs[0], outs[1])
 
 
-def test_gemm_swiglu_epilogue():
+@pytest.mark.parametrize("tile", [None, "256x1", "256p1"])
+def test_gemm_swiglu_epilogue(monkeypatch, tile):
+    if tile:
+        monkeypatch.setenv("OV_GEMM_TILE", tile)
     g = torch.Generator().manual_seed(11)
     M, K, I = 333, 1024, 3072
     x = torch.randn(M, K, generator=g).half()
@@ -262,7 +266,7 @@ def test_gemm_swiglu_epilogue():
     assert (np.abs(got - ref) <= half_ulp(ref) + 1e-4).all()
 
 
-@pytest.mark.parametrize("tile", ["128x1", "256x1"])
+@pytest.mark.parametrize("tile", ["128x1", "256x1", "256p1"])
 def test_gemm_qknorm_rope_epilogue_matches_standalone_math(monkeypatch, tile):
     monkeypatch.setenv("OV_GEMM_TILE", tile)
     g = torch.Generator().manual_seed(12)
