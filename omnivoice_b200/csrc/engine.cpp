@@ -309,8 +309,9 @@ void Engine::Prepare(const ov_conditional_input* inputs, size_t count,
     return cu[a + 1] - cu[a] > cu[b + 1] - cu[b];
   });
   // A CTA takes two 128-query tiles that share each K/V tile (two softmax
-  // groups ping-ponging on the tensor core) when that still fills the GPU;
-  // short batches take one tile per CTA instead, twice the CTAs.
+  // groups ping-ponging on the tensor core); batches short enough that one
+  // tile per CTA still fits in one wave take single tiles (twice the CTAs,
+  // each tile's softmax split over both warpgroups).
   size_t pairs = 0, singles = 0;
   for (size_t q = 0; q < n_seqs_; ++q) {
     const size_t len = static_cast<size_t>(cu[q + 1] - cu[q]);
@@ -318,7 +319,7 @@ void Engine::Prepare(const ov_conditional_input* inputs, size_t count,
     singles += (len + 127) / 128;
   }
   const bool single_tiles = pairs * cfg_.heads < static_cast<size_t>(sms_) &&
-                            singles * cfg_.heads <= 2 * static_cast<size_t>(sms_);
+                            singles * cfg_.heads <= static_cast<size_t>(sms_);
   const int32_t per_item = single_tiles ? 1 : 2;
   std::vector<int32_t> items;
   for (const int32_t q : seq_order) {
