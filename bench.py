@@ -164,12 +164,50 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def measured_peaks():
-    path = ROOT / "MEASURED_PEAKS.json"
-    if path.exists():
-        d = json.loads(path.read_text())
-        return d.get("bf16_tflops"), d.get("hbm_gbs"), "measured"
-    return 1590.0, 6650.0, "fallback"
+# DRAM bytes per launch of each kernel class, from one ncu capture of the
+# default workload (profiles/step_launches_config2.md: dram__bytes_read.sum +
+# dram__bytes_write.sum per launch).
+NCU_TRAFFIC = {
+    ("c2", "gemm_gate_up_swiglu"): 13.89e6,
+    ("c2", "gemm_down_residual"): 12.68e6,
+    ("c2", "gemm_qkv_qknorm_rope"): 9.89e6,
+    ("c2", "attention"): 5.15e6,
+    ("c2", "gemm_o_residual"): 9.31e6,
+}
+TENSOR_CLASSES = ("gemm_qkv_qknorm_rope", "attention", "gemm_o_residual", "gemm_gate_up_swiglu",
+                  "gemm_down_residual", "gemm_audio_head")
+
+
+def roofline(prof, workload, clocks, gemm_flops, gemm_ms):
+    """Roofline of the dominant kernel class of one profiled step: the class
+    with the most device time (CUDA events around each launch of a captured
+    step on the generator's stream).  achieved = its algorithmic FLOPs (or
+    bytes) per launch / its average launch time.  peak = the measured cuBLAS
+    bf16 GEMM rate (burst; the sustained figure when the run was power
+    capped) or the measured copy bandwidth."""
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) \
+        if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    capped = "sw_power_cap" in (clocks or {}).get("reasons", [])
+    if peaks:
+        tensor_peak = peaks.get("bf16_tflops_sustained" if capped else "bf16_tflops")
+        hbm_peak, kind = peaks.get("hbm_gbs"), "measured" + (" (sustained)" if capped else " (burst)")
+    else:
+        tensor_peak, hbm_peak, kind = 1590.0, 6650.0, "fallback"
+    top = max(prof, key=lambda k: k["ms"])
+    launches = max(top["launches"], 1)
+    per_launch_s = top["ms"] / 1e3 / launches
+    if top["name"] in TENSOR_CLASSES:
+        achieved = top["flops"] / launches / per_launch_s / 1e12
+        bound, unit, peak = "tensor", "TFLOP/s", tensor_peak
+    else:
+        achieved = top["bytes"] / launches / per_launch_s / 1e9
+        bound, unit, peak = "hbm", "GB/s", hbm_peak
+    return {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
+            "frac": achieved / peak if peak else None,
+            "traffic": NCU_TRAFFIC.get((workload, top["name"])),
+            "kernel": top["name"], "launches_per_step": top["launches"],
+            "us_per_launch": per_launch_s * 1e6, "peak_kind": kind,
+            "all_gemms_tflops": gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else None}
 
 
 def cpu_baseline(inputs, threads):
@@ -309,9 +347,6 @@ def run_ours(args, rank, world, local_rank, dist):
     gemms = [k for k in prof if k["name"].startswith("gemm")]
     gemm_ms = sum(k["ms"] for k in gemms)
     gemm_flops = sum(k["flops"] for k in gemms)
-    gemm_launches = sum(k["launches"] for k in gemms)
-    tflops_peak, hbm_peak, peak_kind = measured_peaks()
-    achieved = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else 0.0
 
     # End to end through the public API with host buffers: the C-ABI batch
     # call per rank; for the batched workload the data-parallel scheduler
@@ -358,10 +393,7 @@ def run_ours(args, rank, world, local_rank, dist):
                    **extra},
         "backbone_ms_per_step": backbone_ms,
         "full_step_ms": ms_per_gen / max(st.steps_run, 1),
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": tflops_peak,
-                     "unit": "TFLOP/s", "frac": achieved / tflops_peak if tflops_peak else None,
-                     "traffic": None, "kernel": "tcgen05 GEMM (all backbone + head launches)",
-                     "launches_per_step": gemm_launches, "peak_kind": peak_kind},
+        "roofline": roofline(prof, args.workload, clocks.summary(), gemm_flops, gemm_ms),
         "cpu_baseline": base,
         "clocks": clocks.summary(),
         "e2e": {"value": e2e_value, "unit": "audio_s/s",
