@@ -923,7 +923,7 @@ GemmShapeChoice ChooseGemmShape(int M, int N, int K, int epilogue, bool have_wor
         const double rounds = std::ceil(units / ctas);
         double cost = rounds * (static_cast<double>(kblocks) / s) * per_kblock(bn) + kFill;
         if (s > 1)
-          cost += cluster ? 4.0 + (s - 1) * (kBM * (bn / s) * 4.0) / 8192.0 : (s - 1) * 12.0;
+          cost += cluster ? 4.0 + (s - 1) * (kBM * (bn / s) * 4.0) / 8192.0 : (s - 1) * 18.0;
         if (cost < best_cost - 1e-9) {
           best_cost = cost;
           best = {bn, s, cluster};
