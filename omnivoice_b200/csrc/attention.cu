@@ -155,23 +155,33 @@ __device__ __forceinline__ void SoftmaxRole(const AttnArgs& args, const CUtensor
     __syncwarp();  // the tensor-memory accesses below are warp-collective
     tc_fence_after_sync();
     const int valid = min(kKeys, len - t * kKeys);
-    // Pass 1: row maximum (two 32-column chunks in registers at a time;
-    // keys past the sequence end read as -inf).
+    // Pass 1: row maximum, 64 columns in registers at a time, the higher
+    // half first; keys past the sequence end read as -inf.  The lower half
+    // (columns col0 .. col0 + 63) stays in registers for pass 2: P is
+    // written over S columns k / 2, so S columns 32 .. 63 are overwritten
+    // (by this warpgroup in a tile pair, by the other warpgroup of a split
+    // tile once both passed the exchange barrier) and are never read again.
     float mt = -INFINITY;
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      if (half >= halves) break;  // uniform over the CTA
-      const int k0 = col0 + half * 64;
+    uint32_t ka[32], kb[32];
+    if (halves == 2) {
       uint32_t ra[32], rb[32];
-      tmem_ld_32x32b_x32(s_addr + k0, ra);
-      tmem_ld_32x32b_x32(s_addr + k0 + 32, rb);
+      tmem_ld_32x32b_x32(s_addr + col0 + 64, ra);
+      tmem_ld_32x32b_x32(s_addr + col0 + 96, rb);
       tmem_ld_wait();
       if (valid < kKeys) {
-        mask_keys(ra, k0, valid);
-        mask_keys(rb, k0 + 32, valid);
+        mask_keys(ra, col0 + 64, valid);
+        mask_keys(rb, col0 + 96, valid);
       }
-      mt = fmaxf(mt, fmaxf(max32(ra), max32(rb)));
+      mt = fmaxf(max32(ra), max32(rb));
     }
+    tmem_ld_32x32b_x32(s_addr + col0, ka);
+    tmem_ld_32x32b_x32(s_addr + col0 + 32, kb);
+    tmem_ld_wait();
+    if (valid < kKeys) {
+      mask_keys(ka, col0, valid);
+      mask_keys(kb, col0 + 32, valid);
+    }
+    mt = fmaxf(mt, fmaxf(max32(ka), max32(kb)));
     if (split) {
       float* xm = xmax + (t & 1) * 256;
       xm[wg * 128 + row] = mt;
@@ -217,26 +227,31 @@ __device__ __forceinline__ void SoftmaxRole(const AttnArgs& args, const CUtensor
       }
     }
     // Pass 2: probabilities, written as half pairs over the consumed S
-    // columns (key k -> column k / 2).
+    // columns (key k -> column k / 2): the lower half from registers, then
+    // (tile pairs) the higher half, reloaded.
     float rowsum = 0.0f;
     const float neg_m = -m;
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      if (half >= halves) break;  // uniform over the CTA
-      const int k0 = col0 + half * 64;
+    {
+      uint32_t pa[16], pb[16];
+      rowsum += probs32(ka, args.scale_log2, neg_m, pa);
+      rowsum += probs32(kb, args.scale_log2, neg_m, pb);
+      tmem_st_32x32b_x16(s_addr + col0 / 2, pa);
+      tmem_st_32x32b_x16(s_addr + col0 / 2 + 16, pb);
+    }
+    if (halves == 2) {
       uint32_t ra[32], rb[32];
-      tmem_ld_32x32b_x32(s_addr + k0, ra);
-      tmem_ld_32x32b_x32(s_addr + k0 + 32, rb);
+      tmem_ld_32x32b_x32(s_addr + col0 + 64, ra);
+      tmem_ld_32x32b_x32(s_addr + col0 + 96, rb);
       tmem_ld_wait();
       if (valid < kKeys) {
-        mask_keys(ra, k0, valid);
-        mask_keys(rb, k0 + 32, valid);
+        mask_keys(ra, col0 + 64, valid);
+        mask_keys(rb, col0 + 96, valid);
       }
       uint32_t pa[16], pb[16];
       rowsum += probs32(ra, args.scale_log2, neg_m, pa);
       rowsum += probs32(rb, args.scale_log2, neg_m, pb);
-      tmem_st_32x32b_x16(s_addr + k0 / 2, pa);
-      tmem_st_32x32b_x16(s_addr + k0 / 2 + 16, pb);
+      tmem_st_32x32b_x16(s_addr + col0 / 2 + 32, pa);
+      tmem_st_32x32b_x16(s_addr + col0 / 2 + 48, pb);
     }
     l += rowsum;
     tmem_st_wait();
