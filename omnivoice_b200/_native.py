@@ -79,6 +79,14 @@ class EpilogueArgs(Structure):
                 ("epsilon", c_float)]
 
 
+class CodecConfigC(Structure):
+    _fields_ = [("codebooks", c_size_t), ("codebook_size", c_size_t),
+                ("codebook_dim", c_size_t), ("semantic_hidden", c_size_t),
+                ("latent_channels", c_size_t), ("decoder_channels", c_size_t),
+                ("upsampling_ratios", c_size_t * 8), ("num_upsampling", c_size_t),
+                ("sample_rate", c_uint32)]
+
+
 CANCEL_FN = ctypes.CFUNCTYPE(c_int, c_void_p)
 
 _P = c_void_p  # device or host pointer passed as an integer address
@@ -154,6 +162,15 @@ SIGNATURES: dict[str, tuple] = {
     "ov_unmask_schedule": (c_int, [_S, _S, c_float, POINTER(c_size_t)]),
     "ov_build_conditional_input": (c_size_t, [POINTER(c_uint32), _S, POINTER(c_int32), _S, _S,
                                               _S, c_uint32, POINTER(c_int32)]),
+    # ov_codec.h
+    "ov_codec_default_config": (None, [POINTER(CodecConfigC)]),
+    "ov_codec_load": (c_int, [POINTER(CodecConfigC), c_char_p, c_int, POINTER(c_void_p)]),
+    "ov_codec_create_synthetic": (c_int, [POINTER(CodecConfigC), c_uint64, c_int,
+                                          POINTER(c_void_p)]),
+    "ov_codec_free": (None, [_P]),
+    "ov_codec_frame_samples": (c_size_t, [_P]),
+    "ov_codec_decode": (c_int, [_P, _P, _S, _P]),
+    "ov_codec_decode_device": (c_int, [_P, _P, _S, _P, _P]),
 }
 
 _lib: ctypes.CDLL | None = None

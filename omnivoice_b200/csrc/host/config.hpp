@@ -1,5 +1,6 @@
 // The part of the reference's model configuration (config.hpp:14-80) that
-// the generator reads: the backbone shape and the audio codebook layout.
+// the generator and the codec decoder read: the backbone shape, the audio
+// codebook layout and the audio tokenizer's decoder shape.
 // In the reference tree the reference's own config.hpp (which has these
 // members and the codec's) is used instead; the drop-in generator reads
 // only the members declared here.
@@ -8,6 +9,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <vector>
 
 namespace gufo::models::omnivoice {
 
@@ -24,6 +26,38 @@ struct BackboneConfig {
   float rope_theta = 0.0F;
 };
 
+/// config.hpp:28-43: of the semantic (HuBERT) encoder the decoder reads
+/// only the width, which with the acoustic latent width makes the RVQ's
+/// hidden size.
+struct SemanticEncoderConfig {
+  std::size_t hidden_size = 0;
+};
+
+/// config.hpp:45-52 (DAC encoder and decoder of the acoustic branch).
+struct AcousticConfig {
+  std::size_t encoder_channels = 0;
+  std::size_t decoder_channels = 0;
+  std::size_t latent_channels = 0;
+  std::vector<std::size_t> downsampling_ratios;
+  std::vector<std::size_t> upsampling_ratios;
+};
+
+/// config.hpp:54-72 (Higgs Audio v2 tokenizer).
+struct CodecConfig {
+  std::uint32_t sample_rate = 0;
+  std::size_t frame_samples = 0;
+  std::size_t codebooks = 0;
+  std::size_t codebook_size = 0;
+  std::size_t codebook_dim = 0;
+  std::size_t semantic_stride = 0;
+  SemanticEncoderConfig semantic;
+  AcousticConfig acoustic;
+
+  [[nodiscard]] std::uint32_t FrameRate() const {
+    return frame_samples == 0 ? 0 : sample_rate / static_cast<std::uint32_t>(frame_samples);
+  }
+};
+
 struct Config {
   BackboneConfig backbone;
   /// Codebooks the backbone embeds and predicts per audio frame.
@@ -31,6 +65,7 @@ struct Config {
   /// Entries per codebook, including the mask.
   std::size_t audio_vocab_size = 0;
   std::uint32_t audio_mask_id = 0;
+  CodecConfig codec;
 };
 
 }  // namespace gufo::models::omnivoice
