@@ -1,7 +1,7 @@
 """Throughput of OmniVoice's generator hot path on B200.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload c2|c1|c3|c5|c4] [--noise device|reference]
+                  [--workload c2|c1|c3|c5|c4|codec] [--noise device|reference]
 
 A "step" is one full 32-step CFG unmasking generation of the workload.
 The default workload is BASELINE config 2 (120 text tokens + 250 masked
@@ -9,6 +9,8 @@ frames = one 10 s utterance) on every GPU: independent utterances are
 replicated across ranks with no collective on the data path (weak
 scaling).  `--workload c4` runs the batched config (64 utterances,
 partitioned across ranks by longest-processing-time, strong scaling).
+`--workload codec` times the audio tokenizer's decoder instead (codes of a
+250-frame chunk to 24 kHz audio, replicas only).
 
 value: audio seconds generated per second, whole job, inputs resident in
 HBM, device time (CUDA events on the generator's stream, max over ranks).
@@ -410,6 +412,134 @@ def run_ours(args, rank, world, local_rank, dist):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------- codec decoder (f1 row)
+
+CODEC_FRAMES = 250  # one 10 s chunk, the generator's config-2 output
+
+
+def codec_flops(cfg, frames):
+    """Algorithmic float32 FLOPs of one decode (the reference's products,
+    codec.cpp:215-253): fc2 after the codebook sum, every convolution as
+    2 x rows x cout x cin x taps (a transposed one over its input rows)."""
+    lat, hid = cfg.latent_channels, cfg.semantic_hidden + cfg.latent_channels
+    total = 2 * frames * lat * hid
+    rows, ch = frames, cfg.decoder_channels
+    total += 2 * rows * ch * lat * 7
+    for s in cfg.upsampling_ratios:
+        out = ch // 2
+        total += 2 * rows * (2 * s) * out * ch       # ConvTranspose1d, 2 s taps
+        rows *= s
+        total += 3 * (2 * rows * out * out * 7 + 2 * rows * out * out)
+        ch = out
+    return total + 2 * rows * ch * 7
+
+
+def run_codec(args, rank, world):
+    """--workload codec: the audio tokenizer's decoder (codes -> 24 kHz
+    audio) on a 250-frame chunk; replicas only (each rank decodes its own
+    chunk, no collective).  value: audio seconds decoded per second, codes
+    and audio resident in HBM (CUDA events on the decode stream, max over
+    ranks); e2e: through ov_codec_decode with host codes and host audio."""
+    import torch
+
+    from omnivoice_b200.codec import Codec, CodecConfig
+    cfg = CodecConfig()
+    codec = Codec.synthetic(cfg, seed=1)
+    rng = np.random.default_rng(rank)
+    codes_h = rng.integers(0, cfg.codebook_size, (cfg.codebooks, CODEC_FRAMES)).astype(np.int32)
+    codes = torch.from_numpy(codes_h).cuda()
+    audio = torch.empty(CODEC_FRAMES * cfg.frame_samples, device="cuda")
+    # Inputs are 250 x 8 codes; the signals it writes (7.7 M samples x 32
+    # channels x 4 planes in the last block) exceed L2, so no flush.
+    stream = torch.cuda.Stream()
+    for _ in range(max(3, args.warmup)):
+        codec.decode_device(codes, audio, stream.cuda_stream)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(os.environ.get("CUDA_VISIBLE_DEVICES", "0").split(",")[0]) as clocks:
+        e0.record(stream)
+        for _ in range(args.steps):
+            codec.decode_device(codes, audio, stream.cuda_stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        host_audio = codec.decode(codes_h)
+    e2e_s = (time.perf_counter() - t0) / args.steps
+    assert np.isfinite(host_audio).all()
+    seconds = CODEC_FRAMES / FRAME_RATE
+    flops = codec_flops(cfg, CODEC_FRAMES)
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) \
+        if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    tf32_peak = (peaks.get("bf16_tflops") or 1590.0) / 2
+    line = {
+        "metric": "audio-sec decoded per sec (codec decoder, 10 s chunk)",
+        "value": world * seconds / (ms / 1e3), "unit": "audio_s/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (split tf32)",
+        "data": "synthetic codes, random-init decoder weights",
+        "config": {"workload": f"codec decode of {CODEC_FRAMES} frames (8 x 1024 codes) -> "
+                               f"{CODEC_FRAMES * cfg.frame_samples} samples",
+                   "parallelism": f"replicas{world}", "l2": "signals exceed L2, no flush"},
+        "roofline": {"bound": "tensor", "achieved": 3 * flops / (ms / 1e3) / 1e12,
+                     "peak": tf32_peak, "unit": "TFLOP/s",
+                     "frac": 3 * flops / (ms / 1e3) / 1e12 / tf32_peak, "traffic": None,
+                     "note": "tf32 MMA FLOPs (3 products per float32 product) over half the "
+                             "measured bf16 peak (tf32 runs at half the f16 rate)"},
+        "e2e": {"value": seconds / e2e_s, "unit": "audio_s/s",
+                "h2d_bytes_per_step": int(codes_h.nbytes),
+                "d2h_bytes_per_step": int(host_audio.nbytes)},
+        "gpu_launches": args.steps * (3 + 7 * len(cfg.upsampling_ratios)),
+        "clocks": clocks.summary(),
+    }
+    if not args.no_cpu_baseline:
+        from oracle import codec as oc
+        shape = oc.CodecShape()
+        weights = oc.synthetic_weights(shape, 1)
+        sample = rng.integers(0, 1024, (8, 3))
+        t0 = time.perf_counter()
+        oc.decode(weights, shape, sample)
+        per_frame = (time.perf_counter() - t0) / 3
+        line["cpu_baseline"] = {"value": 1 / FRAME_RATE / per_frame, "unit": "audio_s/s",
+                                "cores": os.cpu_count(), "kind": "port",
+                                "sample": "oracle/codec.py (numpy float64) decoding 3 frames, "
+                                          "per-frame time scaled to the chunk"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def run_codec_reference(args, rank):
+    """--impl reference --workload codec: the CPU restatement of the
+    reference decoder (oracle/codec.py, numpy; the reference's own decoder is
+    HIP code) on a bounded sample of the chunk: `steps` decodes of 3 frames,
+    scaled per frame.  Rank 0 only."""
+    if rank != 0:
+        return
+    from oracle import codec as oc
+    shape = oc.CodecShape()
+    weights = oc.synthetic_weights(shape, 1)
+    sample = np.random.default_rng(0).integers(0, 1024, (8, 3))
+    for _ in range(min(args.warmup, 1)):
+        oc.decode(weights, shape, sample)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oc.decode(weights, shape, sample)
+    per_frame = (time.perf_counter() - t0) / args.steps / 3
+    value = 1 / FRAME_RATE / per_frame
+    print(json.dumps({
+        "impl": "reference", "metric": "audio-sec decoded per sec (codec decoder, 10 s chunk)",
+        "value": value, "unit": "audio_s/s", "n_gpus": 0, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": per_frame * CODEC_FRAMES * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic codes, random-init decoder weights",
+        "config": {"workload": f"codec decode of {CODEC_FRAMES} frames, sampled as 3 frames"},
+        "cpu_baseline": {"value": value, "unit": "audio_s/s", "cores": os.cpu_count(),
+                         "kind": "port", "sample": "3-frame decodes, per-frame time scaled"},
+        "e2e": {"value": value, "unit": "audio_s/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0}}), flush=True)
+
+
 def main():
     parser = argparse.ArgumentParser(description=__doc__,
                                      formatter_class=argparse.RawDescriptionHelpFormatter)
@@ -417,7 +547,7 @@ def main():
     parser.add_argument("--steps", type=int, default=20)
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    parser.add_argument("--workload", choices=["c1", "c2", "c3", "c4", "c5"], default="c2")
+    parser.add_argument("--workload", choices=["c1", "c2", "c3", "c4", "c5", "codec"], default="c2")
     parser.add_argument("--noise", choices=["device", "reference"], default="device")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     args = parser.parse_args()
@@ -435,7 +565,12 @@ def main():
                                  device_id=torch.device(f"cuda:{local_rank}"))
         dist = tdist
     try:
-        if args.impl == "reference":
+        if args.workload == "codec":
+            if args.impl == "reference":
+                run_codec_reference(args, rank)
+            else:
+                run_codec(args, rank, world)
+        elif args.impl == "reference":
             run_reference(args, rank, world)
         else:
             run_ours(args, rank, world, local_rank, dist)

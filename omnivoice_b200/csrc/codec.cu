@@ -314,17 +314,19 @@ __global__ void __launch_bounds__(256)
 
 // The output convolution (channels -> 1, kernel 7, codec.cpp:252-253): one
 // thread per sample; the CTA stages its rows plus the 3-row halos of the
-// snake'd input (hi + lo = the float32 value) in shared memory.
+// snake'd input (hi + lo = the float32 value) in shared memory, rows padded
+// by one word so the threads of a warp (consecutive rows) hit distinct banks.
 constexpr int kOutRows = 128;
 constexpr int kOutMaxC = 64;
 __global__ void __launch_bounds__(kOutRows)
     output_conv_kernel(const float* __restrict__ hi, const float* __restrict__ lo, int rows,
                        int channels, const float* __restrict__ weight /* [7][channels] */,
                        const float* __restrict__ bias, float* __restrict__ out) {
-  __shared__ float tile[(kOutRows + 6) * kOutMaxC];
+  __shared__ float tile[(kOutRows + 6) * (kOutMaxC + 1)];
   __shared__ float w[7 * kOutMaxC];
   pdl_wait();
   pdl_trigger();
+  const int stride = channels + 1;
   const int t0 = blockIdx.x * kOutRows;
   for (int i = threadIdx.x; i < 7 * channels; i += kOutRows) w[i] = weight[i];
   for (int i = threadIdx.x; i < (kOutRows + 6) * channels; i += kOutRows) {
@@ -335,14 +337,14 @@ __global__ void __launch_bounds__(kOutRows)
       const int64_t k = static_cast<int64_t>(t) * channels + c;
       v = hi[k] + lo[k];
     }
-    tile[i] = v;
+    tile[r * stride + c] = v;
   }
   __syncthreads();
   const int t = t0 + threadIdx.x;
   if (t >= rows) return;
   float acc = 0.0f;
   for (int k = 0; k < 7; ++k) {
-    const float* row = tile + (threadIdx.x + k) * channels;
+    const float* row = tile + (threadIdx.x + k) * stride;
     const float* wk = w + k * channels;
     for (int c = 0; c < channels; ++c) acc = fmaf(wk[c], row[c], acc);
   }
