@@ -1,7 +1,7 @@
 """Throughput of OmniVoice's generator hot path on B200.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload c2|c1|c3|c5|c4|codec] [--noise device|reference]
+                  [--workload c2|c1|c3|c5|c4|codec|longtext] [--noise device|reference]
 
 A "step" is one full 32-step CFG unmasking generation of the workload.
 The default workload is BASELINE config 2 (120 text tokens + 250 masked
@@ -10,7 +10,9 @@ replicated across ranks with no collective on the data path (weak
 scaling).  `--workload c4` runs the batched config (64 utterances,
 partitioned across ranks by longest-processing-time, strong scaling).
 `--workload codec` times the audio tokenizer's decoder instead (codes of a
-250-frame chunk to 24 kHz audio, replicas only).
+250-frame chunk to 24 kHz audio, replicas only); `--workload longtext` a
+60 s text as four chunks, generated (chunk 0, then chunks 1-3 batched) and
+decoded, beside the reference's chunk-by-chunk order.
 
 value: audio seconds generated per second, whole job, inputs resident in
 HBM, device time (CUDA events on the generator's stream, max over ranks).
@@ -509,6 +511,70 @@ def run_codec(args, rank, world):
         print(json.dumps(line), flush=True)
 
 
+LONGTEXT_CHUNKS = 4        # a 60 s text: four 15 s chunks (synthesizer.cpp:166-178 chunking)
+LONGTEXT_FRAMES = 375
+LONGTEXT_TEXT = 150
+
+
+def run_longtext(args, rank, world):
+    """--workload longtext: one long text as 4 chunks of 375 frames (60 s of
+    audio), generated and decoded by omnivoice_b200.synthesis: chunk 0
+    first (its codes carry the voice), chunks 1-3 as one packed batch, each
+    chunk decoded by the codec.  value: audio seconds per second (device
+    work, wall clock on the host with synchronised calls); the reference's
+    chunk-by-chunk order (synthesizer.cpp:180-207) on the same generator and
+    codec is reported beside it as `sequential`."""
+    import torch
+
+    from omnivoice_b200 import ConditionalInput, DecodingConfig, Generator
+    from omnivoice_b200.codec import Codec, CodecConfig
+    from omnivoice_b200.synthesis import synthesize_chunks, synthesize_chunks_sequential
+    gen = Generator.synthetic(weight_seed=0)
+    codec = Codec.synthetic(CodecConfig(), seed=1)
+    rng = np.random.default_rng(7 + rank)
+    texts = [rng.integers(0, VOCAB, LONGTEXT_TEXT).tolist() for _ in range(LONGTEXT_CHUNKS)]
+
+    def build(i, voice):
+        if voice is not None:
+            return ConditionalInput.build(texts[voice.index] + texts[i], voice.codes,
+                                          LONGTEXT_FRAMES)
+        return ConditionalInput.build(texts[i], None, LONGTEXT_FRAMES)
+
+    dec = DecodingConfig()
+    seconds = LONGTEXT_CHUNKS * LONGTEXT_FRAMES / FRAME_RATE
+
+    def timed(fn):
+        for _ in range(max(1, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            fn()
+        torch.cuda.synchronize()
+        return (time.perf_counter() - t0) / args.steps
+
+    batched = timed(lambda: synthesize_chunks(gen, codec, LONGTEXT_CHUNKS, build, dec, seed=3))
+    sequential = timed(lambda: synthesize_chunks_sequential(gen, codec, LONGTEXT_CHUNKS, build,
+                                                            dec, seed=3))
+    if rank == 0:
+        print(json.dumps({
+            "metric": "audio-sec synthesised per sec (60 s text, 4 chunks, generate + decode)",
+            "value": world * seconds / batched, "unit": "audio_s/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": batched * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16/f32",
+            "data": "synthetic text ids, random-init generator and codec weights",
+            "config": {"workload": f"{LONGTEXT_CHUNKS} chunks x ({LONGTEXT_TEXT} text + "
+                                   f"{LONGTEXT_FRAMES} frames), voice carried from chunk 0",
+                       "parallelism": f"replicas{world}"},
+            "sequential": {"value": world * seconds / sequential, "unit": "audio_s/s",
+                           "ms_per_step": sequential * 1e3,
+                           "note": "the reference's chunk-by-chunk order on the same kernels"},
+            "timing": "host wall clock around synchronised calls (includes host-device copies)"}),
+              flush=True)
+    gen.close()
+    codec.close()
+
+
 def run_codec_reference(args, rank):
     """--impl reference --workload codec: the CPU restatement of the
     reference decoder (oracle/codec.py, numpy; the reference's own decoder is
@@ -547,7 +613,8 @@ def main():
     parser.add_argument("--steps", type=int, default=20)
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    parser.add_argument("--workload", choices=["c1", "c2", "c3", "c4", "c5", "codec"], default="c2")
+    parser.add_argument("--workload", choices=["c1", "c2", "c3", "c4", "c5", "codec", "longtext"],
+                        default="c2")
     parser.add_argument("--noise", choices=["device", "reference"], default="device")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     args = parser.parse_args()
@@ -565,7 +632,15 @@ def main():
                                  device_id=torch.device(f"cuda:{local_rank}"))
         dist = tdist
     try:
-        if args.workload == "codec":
+        if args.workload == "longtext":
+            if args.impl == "reference":
+                if rank == 0:
+                    print(json.dumps({"impl": "reference", "unavailable": "the chunked-synthesis "
+                                      "workload has no CPU arm (its sequential order is timed on "
+                                      "the GPU as `sequential`)"}), flush=True)
+            else:
+                run_longtext(args, rank, world)
+        elif args.workload == "codec":
             if args.impl == "reference":
                 run_codec_reference(args, rank)
             else:
