@@ -33,6 +33,8 @@
 
 #include <cmath>
 #include <cstdint>
+#include <cstdlib>
+#include <cstring>
 
 #include "internal.hpp"
 #include "launch.hpp"
@@ -45,11 +47,14 @@ namespace {
 constexpr int kQ = 128;        // queries per group
 constexpr int kKeys = 128;     // keys per tile
 constexpr int kD = 128;        // head dim
-constexpr int kThreads = 320;  // 2 softmax groups + producer + MMA warp
+// Softmax warpgroups per CTA: 2 (tile pairs, or one tile split in two
+// key halves) or 4 (one tile split in four key quarters); plus a producer
+// and an MMA warp.
+constexpr int ThreadsOf(int wgs) { return 128 * wgs + 64; }
 constexpr uint32_t kHalfTile = 128 * 64 * 2;  // one [128][64] half box: 16 KB
 constexpr uint32_t kTile = 2 * kHalfTile;     // [128][128] half: 32 KB
 // Q0, Q1 | K, V ring of two stages | barriers, row-statistics exchange.
-constexpr uint32_t kSmemBytes = 2 * kTile + 2 * 2 * kTile + 1024 + 4096;
+constexpr uint32_t kSmemBytes = 2 * kTile + 2 * 2 * kTile + 1024 + 8192;
 constexpr float kRescaleThreshold = 8.0f;     // log2 units: P stays below 2^8
 
 // 2^x by the MUFU instruction (relative error far below the half rounding
@@ -118,11 +123,13 @@ struct AttnArgs {
   int kv_heads;
   float scale_log2;  // softmax scale * log2(e)
   uint32_t* err;
+  int single;        // items == null: one 128-query tile per CTA (tile blockIdx.x)
 };
 
-// The softmax warpgroups' part of attention_kernel (see there); kSplit:
-// one query tile shared by both warpgroups.
-template <bool kSplit>
+// The softmax warpgroups' part of attention_kernel (see there); kParts:
+// 1 = each warpgroup owns a query tile, 2 or 4 = kParts warpgroups share
+// one query tile, each taking 128 / kParts key columns and O columns.
+template <int kParts>
 __device__ __forceinline__ void SoftmaxRole(const AttnArgs& args, const CUtensorMap* map_out_p,
                                             uint32_t tmem, uint64_t* s_full, uint64_t* p_full,
                                             uint64_t* o_done, uint64_t* pv_done, float* xmax,
@@ -135,12 +142,14 @@ __device__ __forceinline__ void SoftmaxRole(const AttnArgs& args, const CUtensor
   // ("split"): warpgroup wg takes key columns [64 wg, 64 wg + 64) of every
   // S tile and O columns [64 wg, 64 wg + 64), and the two halves of a row
   // meet in shared memory for the row maximum and the row sum.
-  constexpr bool split = kSplit;
+  constexpr bool split = kParts > 1;
+  constexpr int kCols = 128 / kParts;   // key columns and O columns per warpgroup
+  constexpr int kChunks = kCols / 32;   // 32-column chunks of them
   const int wg = warp >> 2;
   const int g = split ? 0 : wg;
   const int row = (warp & 3) * 32 + lane;
-  const int col0 = split ? 64 * wg : 0;  // first key column and first O column
-  constexpr int halves = split ? 1 : 2;  // 64-column halves handled
+  const int col0 = split ? kCols * wg : 0;  // first key column and first O column
+  constexpr int halves = split ? 1 : 2;     // 64-column halves of keys, upper one reloaded
   const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
   const uint32_t o_addr = tmem + static_cast<uint32_t>(g * 256 + 128) + lane_off;
   float m = -INFINITY, l = 0.0f;
@@ -162,7 +171,7 @@ __device__ __forceinline__ void SoftmaxRole(const AttnArgs& args, const CUtensor
     // (by this warpgroup in a tile pair, by the other warpgroup of a split
     // tile once both passed the exchange barrier) and are never read again.
     float mt = -INFINITY;
-    uint32_t ka[32], kb[32];
+    uint32_t ka[32], kb[kChunks >= 2 ? 32 : 1];
     if (halves == 2) {
       uint32_t ra[32], rb[32];
       tmem_ld_32x32b_x32(s_addr + col0 + 64, ra);
@@ -174,19 +183,28 @@ __device__ __forceinline__ void SoftmaxRole(const AttnArgs& args, const CUtensor
       }
       mt = fmaxf(max32(ra), max32(rb));
     }
-    tmem_ld_32x32b_x32(s_addr + col0, ka);
-    tmem_ld_32x32b_x32(s_addr + col0 + 32, kb);
-    tmem_ld_wait();
-    if (valid < kKeys) {
-      mask_keys(ka, col0, valid);
-      mask_keys(kb, col0 + 32, valid);
+    if constexpr (kChunks >= 2) {
+      tmem_ld_32x32b_x32(s_addr + col0, ka);
+      tmem_ld_32x32b_x32(s_addr + col0 + 32, kb);
+      tmem_ld_wait();
+      if (valid < kKeys) {
+        mask_keys(ka, col0, valid);
+        mask_keys(kb, col0 + 32, valid);
+      }
+      mt = fmaxf(mt, fmaxf(max32(ka), max32(kb)));
+    } else {
+      tmem_ld_32x32b_x32(s_addr + col0, ka);
+      tmem_ld_wait();
+      if (valid < kKeys) mask_keys(ka, col0, valid);
+      mt = max32(ka);
     }
-    mt = fmaxf(mt, fmaxf(max32(ka), max32(kb)));
-    if (split) {
-      float* xm = xmax + (t & 1) * 256;
+    if (split) {  // the row's parts meet in shared memory
+      float* xm = xmax + (t & 1) * (128 * kParts);
       xm[wg * 128 + row] = mt;
-      named_barrier(1, 256);
-      mt = fmaxf(xm[row], xm[128 + row]);
+      named_barrier(1, 128 * kParts);
+      mt = xm[row];
+#pragma unroll
+      for (int q = 1; q < kParts; ++q) mt = fmaxf(mt, xm[q * 128 + row]);
     }
     mt *= args.scale_log2;
     if (t == 0) {
@@ -211,8 +229,7 @@ __device__ __forceinline__ void SoftmaxRole(const AttnArgs& args, const CUtensor
         const float alpha = ex2_approx(m - m_new);
         l *= alpha;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          if (c >= 2 * halves) break;  // uniform over the CTA
+        for (int c = 0; c < kChunks; ++c) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(o_addr + col0 + c * 32, r);
           tmem_ld_wait();
@@ -231,12 +248,16 @@ __device__ __forceinline__ void SoftmaxRole(const AttnArgs& args, const CUtensor
     // (tile pairs) the higher half, reloaded.
     float rowsum = 0.0f;
     const float neg_m = -m;
-    {
+    if constexpr (kChunks >= 2) {
       uint32_t pa[16], pb[16];
       rowsum += probs32(ka, args.scale_log2, neg_m, pa);
       rowsum += probs32(kb, args.scale_log2, neg_m, pb);
       tmem_st_32x32b_x16(s_addr + col0 / 2, pa);
       tmem_st_32x32b_x16(s_addr + col0 / 2 + 16, pb);
+    } else {
+      uint32_t pa[16];
+      rowsum += probs32(ka, args.scale_log2, neg_m, pa);
+      tmem_st_32x32b_x16(s_addr + col0 / 2, pa);
     }
     if (halves == 2) {
       uint32_t ra[32], rb[32];
@@ -260,10 +281,12 @@ __device__ __forceinline__ void SoftmaxRole(const AttnArgs& args, const CUtensor
     if (threadIdx.x == 0 && t == 0) OV_ATRACE(3);
     if (threadIdx.x == 0 && t == nt - 1) OV_ATRACE(4);
   }
-  if (split) {  // row sum = half 0 + half 1
+  if (split) {  // row sum = the sum of the parts, in part order
     xsum[wg * 128 + row] = l;
-    named_barrier(1, 256);
-    l = xsum[row] + xsum[128 + row];
+    named_barrier(1, 128 * kParts);
+    l = xsum[row];
+#pragma unroll
+    for (int q = 1; q < kParts; ++q) l += xsum[q * 128 + row];
   }
   (void)mbar_wait(&o_done[g], 0, args.err);
   __syncwarp();
@@ -277,8 +300,7 @@ __device__ __forceinline__ void SoftmaxRole(const AttnArgs& args, const CUtensor
       // last S MMA, as 128B-swizzled [128][64] boxes, one TMA store each.
       uint8_t* stage = q_s + g * kTile;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        if (c >= 2 * halves) break;  // uniform over the CTA
+      for (int c = 0; c < kChunks; ++c) {
         const int ocol = col0 + c * 32;  // output column of this chunk
         uint32_t r[32];
         tmem_ld_32x32b_x32(o_addr + ocol, r);
@@ -295,8 +317,11 @@ __device__ __forceinline__ void SoftmaxRole(const AttnArgs& args, const CUtensor
         }
       }
       fence_proxy_async_smem();
-      named_barrier(2 + wg, 128);
-      if ((warp & 3) == 0 && lane == 0) {
+      // Each 64-column half is stored once the warpgroups writing it
+      // (one for a tile pair or a 2-way split, two for a 4-way split) have.
+      constexpr int kWgPerHalf = kParts == 4 ? 2 : 1;
+      named_barrier(split ? 2 + (col0 >> 6) : 2 + wg, 128 * kWgPerHalf);
+      if (wg % kWgPerHalf == 0 && (warp & 3) == 0 && lane == 0) {
         for (int b = col0 >> 6; b < (col0 >> 6) + halves; ++b)
           tma_store_2d(map_out_p, stage + b * kHalfTile, h * kD + b * 64, start + tile_row0);
         bulk_commit_group();
@@ -308,8 +333,7 @@ __device__ __forceinline__ void SoftmaxRole(const AttnArgs& args, const CUtensor
       const bool store = tile_row0 + row < len;
       __half* dst = args.out + static_cast<int64_t>(start + tile_row0 + row) * args.ld_out + h * kD;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        if (c >= 2 * halves) break;  // uniform over the CTA
+      for (int c = 0; c < kChunks; ++c) {
         const int ocol = col0 + c * 32;
         uint32_t r[32];
         tmem_ld_32x32b_x32(o_addr + ocol, r);
@@ -330,9 +354,12 @@ __device__ __forceinline__ void SoftmaxRole(const AttnArgs& args, const CUtensor
   }
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+template <int kWG>
+__global__ void __launch_bounds__(ThreadsOf(kWG), 1)
     attention_kernel(const __grid_constant__ CUtensorMap map_qkv,
                      const __grid_constant__ CUtensorMap map_out, const AttnArgs args) {
+  constexpr int kProducerWarp = 4 * kWG;
+  constexpr int kMmaWarp = 4 * kWG + 1;
   if (threadIdx.x == 0) OV_ATRACE(0);
   pdl_wait();
   pdl_trigger();
@@ -342,11 +369,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int code = args.items[2 * blockIdx.x + 1];
     tile = code & 0xFFFFFF;
     max_groups = code >> 24;
+  } else if (args.single) {
+    seq = blockIdx.y;
+    tile = blockIdx.x;
+    max_groups = 1;
   } else {
     seq = blockIdx.y;
     tile = 2 * blockIdx.x;
     max_groups = 2;
   }
+  if (kWG == 4) max_groups = 1;  // the four-warpgroup form takes single tiles only
   const int h = blockIdx.z;
   const int start = args.cu_seqlens[seq];
   const int len = args.cu_seqlens[seq + 1] - start;
@@ -376,8 +408,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* o_done = bars + 13;   // [2 groups]
   uint64_t* pv_done = bars + 15;  // one query tile: each P V complete
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
-  float* xmax = reinterpret_cast<float*>(bars + 18);  // [2 tiles][2 warpgroups][128 rows]
-  float* xsum = xmax + 512;                           // [2 warpgroups][128 rows]
+  float* xmax = reinterpret_cast<float*>(bars + 18);  // [2 tiles][kWG warpgroups][128 rows]
+  float* xsum = xmax + 2 * kWG * 128;                 // [kWG warpgroups][128 rows]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -389,8 +421,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      // One query tile: both softmax warpgroups arrive on p_full[0].
-      mbar_init(&p_full[i], groups == 1 ? 256 : 128);
+      // One query tile: every softmax warpgroup arrives on p_full[i].
+      mbar_init(&p_full[i], groups == 1 ? 128 * kWG : 128);
       mbar_init(&o_done[i], 1);
     }
     mbar_init(pv_done, 1);
@@ -398,7 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_map(&map_qkv);
     tma_prefetch_map(&map_out);
   }
-  if (warp == 9) {
+  if (warp == kMmaWarp) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -408,7 +440,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   if (threadIdx.x == 0) OV_ATRACE(1);
 
-  if (warp == 8) {
+  if (warp == kProducerWarp) {
     // Lane 0 loads Q and the K tiles, lane 1 the V tiles, each into a
     // 2-deep ring; stage t & 1 is refilled once the MMAs reading it are done.
     if (lane < 2) {
@@ -443,7 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = issued > 2 ? issued - 2 : 0; t < issued; ++t)
         (void)mbar_wait(&full[t & 1], static_cast<uint32_t>(t >> 1) & 1u, args.err);
     }
-  } else if (warp == 9) {
+  } else if (warp == kMmaWarp) {
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_f16_f32(kQ, kKeys, 0);
       constexpr uint32_t idesc_o = idesc_f16_f32(kQ, kD, 1);
@@ -566,17 +598,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (more) umma_commit(&k_empty[(t + 1) & 1]);
       }
     }
+  } else if constexpr (kWG == 4) {
+    SoftmaxRole<4>(args, &map_out, tmem, s_full, p_full, o_done, pv_done, xmax, xsum, q_s, warp,
+                   lane, len, nt, q0, start, h);
   } else {
     if (groups == 1)
-      SoftmaxRole<true>(args, &map_out, tmem, s_full, p_full, o_done, pv_done, xmax, xsum, q_s,
-                        warp, lane, len, nt, q0, start, h);
+      SoftmaxRole<2>(args, &map_out, tmem, s_full, p_full, o_done, pv_done, xmax, xsum, q_s,
+                     warp, lane, len, nt, q0, start, h);
     else
-      SoftmaxRole<false>(args, &map_out, tmem, s_full, p_full, o_done, pv_done, xmax, xsum,
-                         q_s, warp, lane, len, nt, q0, start, h);
+      SoftmaxRole<1>(args, &map_out, tmem, s_full, p_full, o_done, pv_done, xmax, xsum, q_s,
+                     warp, lane, len, nt, q0, start, h);
   }
   tc_fence_before_sync();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == kMmaWarp) {
     tc_fence_after_sync();
     tmem_dealloc(tmem, 512);
 #ifdef OV_ATTN_TRACE
@@ -593,19 +628,21 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace
 
 void ConfigureAttentionKernel() {
-  SetMaxDynamicSmem(reinterpret_cast<const void*>(attention_kernel),
+  SetMaxDynamicSmem(reinterpret_cast<const void*>(attention_kernel<2>),
+                    static_cast<int>(kSmemBytes));
+  SetMaxDynamicSmem(reinterpret_cast<const void*>(attention_kernel<4>),
                     static_cast<int>(kSmemBytes));
 }
 
 // items: device [n_items][2] (sequence, first 128-query tile | max groups
-// << 24); null to cover ceil(max_seqlen / 256) tile pairs of every sequence.
+// << 24); null to cover every sequence by tile pairs (ceil(max_seqlen /
+// 256) per sequence) or, `single`, by single tiles (ceil(max_seqlen / 128)).
+// single: every work item is one query tile, run by the four-warpgroup form.
 void LaunchAttention(const CUtensorMap& map_qkv, const CUtensorMap& map_out,
                      const int32_t* cu_seqlens, int num_seqs, int max_seqlen,
                      const int32_t* items, int n_items, int heads, int kv_heads, float scale,
-                     __half* out, int64_t ld_out, cudaStream_t stream) {
+                     __half* out, int64_t ld_out, cudaStream_t stream, bool single) {
   if (num_seqs == 0 || max_seqlen == 0) return;
-  SetMaxDynamicSmem(reinterpret_cast<const void*>(attention_kernel),
-                    static_cast<int>(kSmemBytes));
   AttnArgs a;
   a.cu_seqlens = cu_seqlens;
   a.items = items;
@@ -615,12 +652,23 @@ void LaunchAttention(const CUtensorMap& map_qkv, const CUtensorMap& map_out,
   a.kv_heads = kv_heads;
   a.scale_log2 = scale * 1.4426950408889634f;
   a.err = DeviceErrorWord();
+  a.single = single ? 1 : 0;
+  const int per = single ? kQ : 2 * kQ;
   const dim3 grid = items != nullptr
                         ? dim3(static_cast<unsigned>(n_items), 1, static_cast<unsigned>(heads))
-                        : dim3(static_cast<unsigned>((max_seqlen + 2 * kQ - 1) / (2 * kQ)),
+                        : dim3(static_cast<unsigned>((max_seqlen + per - 1) / per),
                                static_cast<unsigned>(num_seqs), static_cast<unsigned>(heads));
-  Launch(attention_kernel, grid, dim3(kThreads), kSmemBytes, stream, "attention kernel launch",
-         map_qkv, map_out, a);
+  if (single) {
+    SetMaxDynamicSmem(reinterpret_cast<const void*>(attention_kernel<4>),
+                      static_cast<int>(kSmemBytes));
+    Launch(attention_kernel<4>, grid, dim3(ThreadsOf(4)), kSmemBytes, stream,
+           "attention kernel launch", map_qkv, map_out, a);
+  } else {
+    SetMaxDynamicSmem(reinterpret_cast<const void*>(attention_kernel<2>),
+                      static_cast<int>(kSmemBytes));
+    Launch(attention_kernel<2>, grid, dim3(ThreadsOf(2)), kSmemBytes, stream,
+           "attention kernel launch", map_qkv, map_out, a);
+  }
 }
 
 void EncodeAttnOutMap(CUtensorMap* map, const uint16_t* out, int64_t ld_out, int64_t rows,
@@ -671,9 +719,18 @@ extern "C" int ov_attention_varlen(const uint16_t* qkv, size_t ld_qkv, size_t ro
                  static_cast<int64_t>((heads + 2 * kv_heads) * head_dim));
     EncodeAttnOutMap(&map_out, out, static_cast<int64_t>(ld_out), static_cast<int64_t>(rows),
                      static_cast<int64_t>(heads * head_dim));
+    // Single query tiles (four softmax warpgroups each) when one tile per
+    // CTA still fits the GPU in one wave, else tile pairs; OV_ATTN_FORM =
+    // single | pair in the environment overrides (tuning and test aid).
+    const size_t tiles = (max_seqlen + 127) / 128 * num_seqs * heads;
+    bool single = tiles <= static_cast<size_t>(SmCount());
+    if (const char* env = std::getenv("OV_ATTN_FORM")) {
+      if (std::strcmp(env, "single") == 0) single = true;
+      if (std::strcmp(env, "pair") == 0) single = false;
+    }
     LaunchAttention(map, map_out, cu_seqlens, static_cast<int>(num_seqs), static_cast<int>(max_seqlen),
                     nullptr, 0, static_cast<int>(heads), static_cast<int>(kv_heads), scale,
                     reinterpret_cast<__half*>(out), static_cast<int64_t>(ld_out),
-                    AsStream(stream));
+                    AsStream(stream), single);
   });
 }

@@ -311,15 +311,16 @@ void Engine::Prepare(const ov_conditional_input* inputs, size_t count,
   // A CTA takes two 128-query tiles that share each K/V tile (two softmax
   // groups ping-ponging on the tensor core); batches short enough that one
   // tile per CTA still fits in one wave take single tiles (twice the CTAs,
-  // each tile's softmax split over both warpgroups).
+  // each tile's softmax split over four warpgroups).
   size_t pairs = 0, singles = 0;
   for (size_t q = 0; q < n_seqs_; ++q) {
     const size_t len = static_cast<size_t>(cu[q + 1] - cu[q]);
     pairs += (len + 255) / 256;
     singles += (len + 127) / 128;
   }
-  const bool single_tiles = pairs * cfg_.heads < static_cast<size_t>(sms_) &&
-                            singles * cfg_.heads <= static_cast<size_t>(sms_);
+  single_tiles_ = pairs * cfg_.heads < static_cast<size_t>(sms_) &&
+                  singles * cfg_.heads <= static_cast<size_t>(sms_);
+  const bool single_tiles = single_tiles_;
   const int32_t per_item = single_tiles ? 1 : 2;
   std::vector<int32_t> items;
   for (const int32_t q : seq_order) {
@@ -533,7 +534,8 @@ void Engine::EnqueueForward(cudaStream_t s, Marker* m) {
                     static_cast<int>(max_seqlen_), attn_items_.get(),
                     static_cast<int>(n_items_), static_cast<int>(cfg_.heads),
                     static_cast<int>(cfg_.kv_heads), scale,
-                    reinterpret_cast<__half*>(attn_.get()), static_cast<int64_t>(QH_), s);
+                    reinterpret_cast<__half*>(attn_.get()), static_cast<int64_t>(QH_), s,
+                    single_tiles_);
     mark(kGemmO, 2.0 * R * QH_ * H, 0.0);
     LaunchGemm(p.o, s);
     mark(kRmsNorm, 0.0, norm_bytes);

@@ -111,6 +111,7 @@ class Engine {
   DeviceBuffer<int32_t> ids_, ids_init_, positions_, row_text_, cu_seqlens_, targets_;
   DeviceBuffer<int32_t> frame_utt_, counts_, step_list_d_, launch_;
   DeviceBuffer<int32_t> attn_items_;  // [n_items][2] (sequence, query-tile pair)
+  bool single_tiles_ = false;         // attention items are single query tiles
   size_t n_items_ = 0;
   DeviceBuffer<UttDesc> utts_d_;
   DeviceBuffer<float> gumbel_;

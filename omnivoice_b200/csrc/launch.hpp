@@ -86,7 +86,7 @@ void EncodeAttnOutMap(CUtensorMap* map, const uint16_t* out, int64_t ld_out, int
 void LaunchAttention(const CUtensorMap& map_qkv, const CUtensorMap& map_out,
                      const int32_t* cu_seqlens, int num_seqs, int max_seqlen,
                      const int32_t* items, int n_items, int heads, int kv_heads, float scale,
-                     __half* out, int64_t ld_out, cudaStream_t stream);
+                     __half* out, int64_t ld_out, cudaStream_t stream, bool single = false);
 
 void LaunchScore(const float* logits, int64_t ld, int total_frames, int codebooks, int vocab,
                  uint32_t mask_id, float guidance, const UttDesc* utts, const int32_t* frame_utt,
