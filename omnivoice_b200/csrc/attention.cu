@@ -361,7 +361,9 @@ __global__ void __launch_bounds__(ThreadsOf(kWG), 1)
   constexpr int kProducerWarp = 4 * kWG;
   constexpr int kMmaWarp = 4 * kWG + 1;
   if (threadIdx.x == 0) OV_ATRACE(0);
-  pdl_wait();
+  // The next kernel may start its prologue now; this one waits for its
+  // inputs (q, k, v of the previous kernel) only after its own set-up.  The
+  // work items and sequence bounds are uploaded before the step.
   pdl_trigger();
   int seq, tile, max_groups;
   if (args.items != nullptr) {
@@ -438,6 +440,7 @@ __global__ void __launch_bounds__(ThreadsOf(kWG), 1)
   __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();  // q, k, v of the previous kernel are complete
   if (threadIdx.x == 0) OV_ATRACE(1);
 
   if (warp == kProducerWarp) {

@@ -63,8 +63,8 @@ __global__ void __launch_bounds__(kScoreWarps * 32)
                  int vocab, uint32_t mask_id, float guidance, const UttDesc* __restrict__ utts,
                  const int32_t* __restrict__ frame_utt, int single_frames,
                  int32_t* __restrict__ prediction, float* __restrict__ confidence) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t item = static_cast<int64_t>(blockIdx.x) * kScoreWarps + (threadIdx.x >> 5);
   if (item >= static_cast<int64_t>(total_frames) * codebooks) return;
@@ -192,8 +192,8 @@ __global__ void __launch_bounds__(kSelectThreads)
   __shared__ int s_total;
   __shared__ uint32_t s_digit;
   __shared__ int s_remaining;
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int tid = threadIdx.x;
   const UttDesc d = table != nullptr ? table[blockIdx.x] : single;
   const int frames = d.frames;

@@ -62,8 +62,8 @@ __global__ void __launch_bounds__(kRowsPerBlock * 32)
                  float* __restrict__ hidden, const float* __restrict__ norm_weight,
                  float epsilon, __half* __restrict__ normed, uint32_t* err) {
   constexpr int width = 128 * kVec;
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kRowsPerBlock + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -112,8 +112,8 @@ __global__ void __launch_bounds__(kRowsPerBlock * 32)
                    int64_t rows, const float* __restrict__ weight, __half* __restrict__ output,
                    float epsilon) {
   constexpr int width = 128 * kVec;
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kRowsPerBlock + (threadIdx.x >> 5);
   if (row >= rows) return;

@@ -507,6 +507,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   if (threadIdx.x == 0) OV_TRACE(0);
+  // The next kernel may start its prologue (its CTAs find SMs only as this
+  // grid's leave); every read of this kernel's inputs waits below.
+  pdl_trigger();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -547,10 +550,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after_sync();
   const uint32_t tmem = *tmem_slot;
   if (threadIdx.x == 0) OV_TRACE(1);
-  if (!(warp == 0 && lane == 0)) {
-    pdl_wait();  // inputs of the previous kernel in the stream are ready
-    pdl_trigger();
-  }
+  if (!(warp == 0 && lane == 0)) pdl_wait();  // inputs of the previous kernel are ready
 
   if (warp == 0) {
     if (lane == 0) {
@@ -587,7 +587,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       pdl_wait();
-      pdl_trigger();
       OV_TRACE(2);
       uint32_t k_iter = 0;
       bool ok = true;
