@@ -110,14 +110,16 @@ typedef struct {
  * x, w are K-major with row strides ldx / in elements (multiples of 8);
  * y's row stride ldy is in elements of the output type.  Short-M products
  * with the residual or plain-store epilogue may be split along K across a
- * thread-block cluster; the splits' partials are summed in split order
- * through distributed shared memory, so results do not depend on timing.
- * `workspace` (optional, may be NULL) additionally allows a serialised
- * split-K: it holds one order counter per output tile
- * (ov_gemm_workspace_bytes gives its size, 0 when the chosen shape needs
- * none), the splits of a tile add into y in split order.  Zero the
- * workspace once before its first use (every call leaves it zero again);
- * calls sharing a workspace must not overlap. */
+ * thread-block cluster; the splits' partials are summed in split order, so
+ * results do not depend on timing.  `workspace` (optional, may be NULL,
+ * 16-byte aligned) lets the splits exchange their partials through global
+ * memory instead of distributed shared memory (faster), and allows a
+ * serialised split-K whose splits add into y in split order behind one
+ * order counter per output tile.  ov_gemm_workspace_bytes gives the size
+ * the chosen shape needs (0: none); with a smaller workspace the call
+ * chooses as if it had none.  Zero the workspace once before its first
+ * use (every call leaves the counters zero again); calls sharing a
+ * workspace must not overlap. */
 int ov_gemm_f16(const uint16_t* x, size_t ldx, const uint16_t* w, void* y, size_t ldy,
                 size_t rows, size_t in, size_t out, int epilogue,
                 const ov_epilogue_args* args, void* workspace, size_t workspace_bytes,
@@ -141,8 +143,9 @@ int ov_interleave_gate_up(const uint16_t* gate_up, size_t width, size_t in, uint
  *   - The first call on a device sets up that device (looks up the array's
  *     device address with that device current and clears its counters);
  *     make that first call before any stream capture.
- *   - Products that would need more than 64 KiB of split-K scratch are
- *     rejected with OV_ERR_INVALID (none do on a 148-SM B200).
+ *   - Products whose preferred split-K form needs more than 64 KiB of
+ *     scratch (cluster split-K exchanging its partials through global
+ *     memory) run as ov_gemm_f16 would without a workspace.
  *   - Every call shares the array, which keeps the last call's contents:
  *     calls that overlap on the GPU (different streams, or different host
  *     threads on one device) race and must be serialised by the caller. */

@@ -478,6 +478,136 @@ __device__ unsigned long long g_gemm_trace[1024 * 16];
   } while (0)
 #endif
 
+// Cluster split-K through global memory (args.xchg set): each rank writes
+// the other ranks' column slices of its partial to the workspace, then
+// arrives (release, cluster scope) on each peer's inbox barrier; rank r
+// waits for the S - 1 arrivals and sums slice r in split order, its own
+// part from tensor memory.  No rank writes into another's shared memory,
+// so nothing waits for a peer's ring to be free or for its copies to be
+// read.  Workspace slot (tile, sender j, slice r): 128 x BN / S floats as
+// [32-column chunk][16-byte piece q][row][4 floats], so a warp's accesses
+// to one piece are 512 contiguous bytes.
+template <int BN, int S>
+__device__ __forceinline__ void XchgSend(const GemmArgs& a, uint32_t tacc, const EpilogueCtx& c,
+                                         int tile, int rank) {
+  constexpr int kCols = BN / S;
+  constexpr int kSlot4 = kBM * kCols / 4;  // float4s per slot
+  constexpr int kPer = kCols / 32;         // 32-column chunks per slice
+  constexpr int kChunks = (S - 1) * kPer;  // chunks sent; group g sends g, g + 2, ...
+  float4* base = reinterpret_cast<float4*>(a.xchg) + (static_cast<size_t>(tile) * S + rank) * S * kSlot4;
+  // Chunk ch: slice of peer p = ch / kPer (split j = p, or p + 1 past this
+  // rank), columns (ch % kPer) * 32 of the slice.
+  auto column = [&](int ch) {
+    const int p = ch / kPer;
+    return (p < rank ? p : p + 1) * kCols + (ch % kPer) * 32;
+  };
+  uint32_t v[2][32];
+  if (c.group < kChunks) {
+    tmem_ld_32x32b_x32(tacc + static_cast<uint32_t>(column(c.group)), v[0]);
+    tmem_ld_wait();
+  }
+#pragma unroll
+  for (int i = 0; i < (kChunks + 1) / 2; ++i) {
+    const int ch = 2 * i + c.group;
+    if (ch >= kChunks) break;  // uniform over the group
+    const int next = ch + 2;
+    if (next < kChunks) tmem_ld_32x32b_x32(tacc + static_cast<uint32_t>(column(next)), v[(i + 1) & 1]);
+    const int col = column(ch);
+    float4* dst = base + (col / kCols) * kSlot4 + ((col % kCols) / 32) * 8 * kBM + c.row;
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      __stcg(dst + q * kBM,
+             make_float4(__uint_as_float(v[i & 1][4 * q]), __uint_as_float(v[i & 1][4 * q + 1]),
+                         __uint_as_float(v[i & 1][4 * q + 2]), __uint_as_float(v[i & 1][4 * q + 3])));
+    if (next < kChunks) tmem_ld_wait();
+  }
+}
+
+// Adds this rank's own part (from tensor memory) into acc.
+__device__ __forceinline__ void AddOwn(float (&acc)[32], uint32_t taddr) {
+  uint32_t own[32];
+  tmem_ld_32x32b_x32(taddr, own);
+  tmem_ld_wait();
+#pragma unroll
+  for (int e = 0; e < 32; ++e) acc[e] += __uint_as_float(own[e]);
+}
+
+template <int BN, int EPI, int S>
+__device__ __forceinline__ void XchgReduce(const GemmArgs& a, const CUtensorMap* map_y,
+                                           EpilogueCtx& c, uint32_t tacc, int tile, int m_tile,
+                                           int n_tile, int rank) {
+  constexpr int kCols = BN / S;
+  constexpr int kSlot4 = kBM * kCols / 4;
+  constexpr int kPeers = S - 1;
+  constexpr int kBatch = kPeers < 2 ? kPeers : 2;  // peers' loads in flight together
+  const float4* slots =
+      reinterpret_cast<const float4*>(a.xchg) + static_cast<size_t>(tile) * S * S * kSlot4;
+  const int y0 = m_tile * kBM;
+#pragma unroll 1
+  for (int cc = 32 * c.group; cc < kCols; cc += 64) {
+    const int x = n_tile * BN + rank * kCols + cc;
+    if (x >= a.out_cols) break;  // uniform over the group
+    const uint32_t own = tacc + static_cast<uint32_t>(rank * kCols + cc);
+    float acc[32];
+#pragma unroll
+    for (int e = 0; e < 32; ++e) acc[e] = 0.0f;
+    // Peer p is split j = p (p < rank) or p + 1; the own part goes between
+    // peers rank - 1 and rank, so the sum runs in split order.
+#pragma unroll
+    for (int p0 = 0; p0 < kPeers; p0 += kBatch) {
+      float4 t[kBatch][8];
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) {
+        const int p = p0 + b;
+        if (p >= kPeers) break;
+        const int j = p < rank ? p : p + 1;
+        const float4* src = slots + (j * S + rank) * kSlot4 + (cc / 32) * 8 * kBM + c.row;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) t[b][q] = __ldcg(src + q * kBM);
+      }
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) {
+        const int p = p0 + b;
+        if (p >= kPeers) break;
+        if (p == rank) AddOwn(acc, own);  // uniform over the CTA
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          acc[4 * q] += t[b][q].x;
+          acc[4 * q + 1] += t[b][q].y;
+          acc[4 * q + 2] += t[b][q].z;
+          acc[4 * q + 3] += t[b][q].w;
+        }
+      }
+    }
+    if (rank == kPeers) AddOwn(acc, own);
+    uint32_t w[32];
+#pragma unroll
+    for (int e = 0; e < 32; ++e) w[e] = __float_as_uint(acc[e]);
+    EmitGroup<EPI == OV_EPI_ACCUM_F32>(c, map_y, w, x, y0, cc / 32);
+  }
+}
+
+template <int BN, int EPI, int S>
+__device__ __forceinline__ void XchgSplitK(const GemmArgs& a, const CUtensorMap* map_y,
+                                           EpilogueCtx& c, uint32_t tacc, uint64_t* inbox_bar,
+                                           int tile, int m_tile, int n_tile, int rank) {
+  if constexpr (BN / S >= 32) {
+    XchgSend<BN, S>(a, tacc, c, tile, rank);
+    named_barrier(kEpiBarrier, 256);  // every partial slice is written
+    if (c.ep == 0) {
+      __threadfence();
+      for (int j = 0; j < S; ++j)
+        if (j != rank) mbar_arrive_cluster(mapa_shared(smem_u32(inbox_bar), static_cast<uint32_t>(j)));
+    }
+    (void)mbar_wait_cluster(inbox_bar, 0, a.err);
+    __syncwarp();
+    if (c.ep == 0) OV_TRACE(14);
+    XchgReduce<BN, EPI, S>(a, map_y, c, tacc, tile, m_tile, n_tile, rank);
+    if (c.ep == 0) OV_TRACE(15);
+  }
+}
+
+
 template <int BN, int EPI, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
@@ -521,7 +651,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       // PAIR: one arrival from each CTA's epilogue (on rank 0's barrier).
       mbar_init(&tempty[b], PAIR ? 2 : 256);
     }
-    mbar_init(inbox_bar, 1);
+    // Global-memory exchange: one arrival per peer; else one arrival that
+    // expects the peers' bulk-copy bytes.
+    mbar_init(inbox_bar, args.xchg != nullptr ? static_cast<uint32_t>(args.splits - 1) : 1u);
     fence_mbar_init();
     tma_prefetch_map(&map_a);
     tma_prefetch_map(&map_b);
@@ -548,6 +680,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   else
     __syncthreads();
   tc_fence_after_sync();
+  // Global-memory split-K exchange: the arrival half of the barrier that
+  // makes every rank's inbox barrier visible before a peer signals it; the
+  // wait half runs after the MMAs, by when every rank has long arrived.
+  if (kClusterSplit && args.xchg != nullptr) cluster_arrive();
   const uint32_t tmem = *tmem_slot;
   if (threadIdx.x == 0) OV_TRACE(1);
   if (!(warp == 0 && lane == 0)) pdl_wait();  // inputs of the previous kernel are ready
@@ -624,10 +760,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           (void)mbar_wait(&full[i % kStages], (i / kStages) & 1u, args.err);
       }
     }
-    if (kClusterSplit && args.cluster) {  // the two barriers of the split-K reduction
+    if (kClusterSplit && args.cluster) {  // the barriers of the split-K reduction
       __syncwarp();
-      cluster_sync();
-      cluster_sync();
+      if (args.xchg != nullptr) {
+        cluster_wait();
+      } else {
+        cluster_sync();
+        cluster_sync();
+      }
     }
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {  // PAIR: rank 0 issues for both CTAs
@@ -684,8 +824,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (kClusterSplit && args.cluster) {
       __syncwarp();
-      cluster_sync();
-      cluster_sync();
+      if (args.xchg != nullptr) {
+        cluster_wait();
+      } else {
+        cluster_sync();
+        cluster_sync();
+      }
     }
   } else {
     EpilogueCtx c;
@@ -698,6 +842,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     c.gep = c.ep & 127;
     const int quarter = warp & 3;  // tensor-memory lanes 32*quarter .. +31
     c.row = quarter * 32 + lane;
+    // Global-memory split-K exchange: every rank's inbox barrier is
+    // initialised before this rank signals it (the wait half of the
+    // prologue's cluster barrier, taken while the MMAs run).
+    if (kClusterSplit && args.xchg != nullptr) cluster_wait();
     int acc_iter = 0;
     for (int u = unit0; u < args.units; u += ustep, ++acc_iter) {
       int m_tile, n_tile, split;
@@ -760,23 +908,40 @@ __global__ void __launch_bounds__(kThreads, 1)
         UnitCoords(args, blockIdx.x, m_tile, n_tile, split);
         const uint32_t tacc = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
         __syncwarp();
-        tc_fence_before_sync();
-        cluster_sync();
-        tc_fence_after_sync();
-        if (c.ep == 0) OV_TRACE(12);
-        if (c.ep == 0) {
-          const uint32_t slot_bytes = static_cast<uint32_t>(kBM * (BN / args.splits) * 4);
-          mbar_arrive_expect_tx(inbox_bar, static_cast<uint32_t>(args.splits - 1) * slot_bytes);
+        if (args.xchg != nullptr) {
+          if (c.ep == 0) OV_TRACE(12);
+          c.ring = smem;  // all MMAs are complete: the idle ring stages the stores
+          const int tile = static_cast<int>(blockIdx.x) / args.splits;
+          switch (args.splits) {
+            case 2:
+              XchgSplitK<BN, EPI, 2>(args, &map_y, c, tacc, inbox_bar, tile, m_tile, n_tile, split);
+              break;
+            case 4:
+              XchgSplitK<BN, EPI, 4>(args, &map_y, c, tacc, inbox_bar, tile, m_tile, n_tile, split);
+              break;
+            default:
+              XchgSplitK<BN, EPI, 8>(args, &map_y, c, tacc, inbox_bar, tile, m_tile, n_tile, split);
+              break;
+          }
+        } else {
+          tc_fence_before_sync();
+          cluster_sync();
+          tc_fence_after_sync();
+          if (c.ep == 0) OV_TRACE(12);
+          if (c.ep == 0) {
+            const uint32_t slot_bytes = static_cast<uint32_t>(kBM * (BN / args.splits) * 4);
+            mbar_arrive_expect_tx(inbox_bar, static_cast<uint32_t>(args.splits - 1) * slot_bytes);
+          }
+          ClusterSend<BN>(tacc, smem, c, split, args.splits, inbox_bar);
+          (void)mbar_wait(inbox_bar, 0, args.err);
+          __syncwarp();
+          if (c.ep == 0) OV_TRACE(14);
+          ClusterReduce<BN, EPI>(args, &map_y, c, tacc, smem, m_tile, n_tile, split);
+          if (c.ep == 0) OV_TRACE(15);
+          // No CTA leaves while a peer's bulk copy may still read its outbox.
+          __syncwarp();
+          cluster_sync();
         }
-        ClusterSend<BN>(tacc, smem, c, split, args.splits, inbox_bar);
-        (void)mbar_wait(inbox_bar, 0, args.err);
-        __syncwarp();
-        if (c.ep == 0) OV_TRACE(14);
-        ClusterReduce<BN, EPI>(args, &map_y, c, tacc, smem, m_tile, n_tile, split);
-        if (c.ep == 0) OV_TRACE(15);
-        // No CTA leaves while a peer's bulk copy may still read its outbox.
-        __syncwarp();
-        cluster_sync();
         if (c.ep == 0) OV_TRACE(6);
       }
     }
@@ -839,16 +1004,17 @@ void LaunchTyped(const GemmPlan& p, cudaStream_t stream) {
 
 int Tiles(int M, int N, int bn) { return ((M + kBM - 1) / kBM) * ((N + bn - 1) / bn); }
 
-bool ValidShape(int bn, int splits, bool cluster, int N, int K, int epilogue) {
+bool ValidShape(int bn, int splits, bool cluster, int N, int K, int epilogue, bool xchg = false) {
   if (splits < 1 || splits > 8) return false;
   if (cluster) {
-    // Split-K inside a thread-block cluster: the splits' partials meet in
-    // distributed shared memory, each rank reducing a BN / splits slice.
+    // Split-K inside a thread-block cluster, each rank reducing a BN /
+    // splits slice of the splits' partials.
     if (splits != 2 && splits != 4 && splits != 8) return false;
     if (epilogue != OV_EPI_ACCUM_F32 && epilogue != OV_EPI_STORE_F32) return false;
     if (bn / splits < 32 || (K / kBK) < splits) return false;
-    // Inbox and outbox, (S - 1) slices each, live in the 192 KB operand ring.
-    if (2 * (splits - 1) * kBM * (bn / splits) * 4 > kRingBytes) return false;
+    // Distributed shared memory: inbox and outbox, (S - 1) slices each,
+    // live in the 192 KB operand ring.
+    if (!xchg && 2 * (splits - 1) * kBM * (bn / splits) * 4 > kRingBytes) return false;
     return bn == 64 || bn == 128 || bn == 256;
   }
   if (splits > 1 && (epilogue != OV_EPI_ACCUM_F32 || (K / kBK) / splits < 2)) return false;
@@ -892,9 +1058,9 @@ GemmShapeChoice ChooseGemmShape(int M, int N, int K, int epilogue, bool have_wor
       const bool cluster = sep == 'c';
       if (sep == 'p') {
         if (ValidPairShape(bn, N, epilogue)) return {bn, 1, false, true};
-      } else if (ValidShape(bn, splits, cluster, N, K, epilogue) &&
+      } else if (ValidShape(bn, splits, cluster, N, K, epilogue, cluster && have_workspace) &&
                  (splits == 1 || cluster || have_workspace)) {
-        return {bn, splits, cluster && splits > 1};
+        return {bn, splits, cluster && splits > 1, false, cluster && splits > 1 && have_workspace};
       }
     }
   }
@@ -904,7 +1070,9 @@ GemmShapeChoice ChooseGemmShape(int M, int N, int K, int epilogue, bool have_wor
   // ceil(units / CTAs) units back to back; each kernel pays a fill
   // (prologue, first loads, last epilogue, about 5 us); serialised split-K
   // adds one tile reduction per extra split; cluster split-K one exchange
-  // of (S - 1) slices through distributed shared memory.
+  // of (S - 1) slices, through the workspace in global memory when there
+  // is one (written and read back at L2 speed), else through distributed
+  // shared memory (about 25 GB/s per SM, measured).
   const int kblocks = K / kBK;
   auto per_kblock = [](int bn) { return bn == 256 ? 1.03 : 1.0; };
   constexpr double kFill = 17.0;
@@ -915,17 +1083,19 @@ GemmShapeChoice ChooseGemmShape(int M, int N, int K, int epilogue, bool have_wor
       for (int cl = 0; cl < 2; ++cl) {
         const bool cluster = cl == 1;
         if (cluster && s == 1) continue;
-        if (!ValidShape(bn, s, cluster, N, K, epilogue)) continue;
+        const bool xchg = cluster && have_workspace;
+        if (!ValidShape(bn, s, cluster, N, K, epilogue, xchg)) continue;
         if (s > 1 && !cluster && (!have_workspace || s > 4)) continue;
         const double units = static_cast<double>(Tiles(M, N, bn)) * s;
         const double ctas = cluster ? ClusterCapacity(s, sms) : sms;
         const double rounds = std::ceil(units / ctas);
         double cost = rounds * (static_cast<double>(kblocks) / s) * per_kblock(bn) + kFill;
-        if (s > 1)
-          cost += cluster ? 4.0 + (s - 1) * (kBM * (bn / s) * 4.0) / 8192.0 : (s - 1) * 18.0;
+        const double slice_bytes = (s - 1) * (kBM * (bn / s) * 4.0);
+        if (s > 1 && !cluster) cost += (s - 1) * 18.0;
+        if (s > 1 && cluster) cost += xchg ? 2.0 + 2.0 * slice_bytes / 49152.0 : 4.0 + slice_bytes / 8192.0;
         if (cost < best_cost - 1e-9) {
           best_cost = cost;
-          best = {bn, s, cluster};
+          best = {bn, s, cluster, false, xchg};
         }
       }
     }
@@ -943,10 +1113,19 @@ GemmShapeChoice ChooseGemmShape(int M, int N, int K, int epilogue, bool have_wor
   return best;
 }
 
+namespace {
+
+size_t WorkspaceNeed(int M, int N, const GemmShapeChoice& c) {
+  if (c.splits <= 1 || (c.cluster && !c.xchg)) return 0;
+  const size_t tiles = static_cast<size_t>(Tiles(M, N, c.bn));
+  if (c.cluster) return tiles * static_cast<size_t>(c.splits) * kBM * c.bn * sizeof(float);
+  return tiles * sizeof(uint32_t);
+}
+
+}  // namespace
+
 size_t GemmWorkspaceBytes(int M, int N, int K, int epilogue, int sms) {
-  const GemmShapeChoice c = ChooseGemmShape(M, N, K, epilogue, true, sms);
-  if (c.splits <= 1 || c.cluster) return 0;
-  return static_cast<size_t>(Tiles(M, N, c.bn)) * sizeof(uint32_t);
+  return WorkspaceNeed(M, N, ChooseGemmShape(M, N, K, epilogue, true, sms));
 }
 
 void PlanGemm(GemmPlan* plan, const uint16_t* x, int64_t ldx, const uint16_t* w, int64_t w_rows,
@@ -960,10 +1139,12 @@ void PlanGemm(GemmPlan* plan, const uint16_t* x, int64_t ldx, const uint16_t* w,
   const bool half_out = epilogue == OV_EPI_SWIGLU_F16 || epilogue == OV_EPI_QKNORM_ROPE_F16;
   OV_REQUIRE(ldy % (half_out ? 8 : 4) == 0, "y row stride must be a multiple of 16 bytes");
   OV_REQUIRE((reinterpret_cast<uintptr_t>(y) & 15u) == 0, "y must be 16-byte aligned");
-  GemmShapeChoice choice =
-      ChooseGemmShape(M, N, K, epilogue, workspace != nullptr && workspace_bytes > 0, sms);
-  if (choice.splits > 1 && !choice.cluster &&
-      workspace_bytes < static_cast<size_t>(Tiles(M, N, choice.bn)) * sizeof(uint32_t))
+  // A workspace too small (or, for the partial slices, not 16-byte
+  // aligned) for the chosen split-K form: choose again without one.
+  const bool ws_ok = workspace != nullptr && workspace_bytes > 0;
+  GemmShapeChoice choice = ChooseGemmShape(M, N, K, epilogue, ws_ok, sms);
+  if (workspace_bytes < WorkspaceNeed(M, N, choice) ||
+      (choice.xchg && (reinterpret_cast<uintptr_t>(workspace) & 15u) != 0))
     choice = ChooseGemmShape(M, N, K, epilogue, false, sms);
   int out_cols = N;
   if (epilogue == OV_EPI_SWIGLU_F16) {
@@ -997,6 +1178,7 @@ void PlanGemm(GemmPlan* plan, const uint16_t* x, int64_t ldx, const uint16_t* w,
   a.err = err != nullptr ? err : DeviceErrorWord();
   if (choice.splits > 1 && !choice.cluster) a.counters = static_cast<uint32_t*>(workspace);
   a.cluster = choice.cluster ? 1 : 0;
+  if (choice.xchg) a.xchg = static_cast<float*>(workspace);
   plan->cluster_x = choice.cluster ? static_cast<unsigned>(choice.splits) : 1u;
   if (ea != nullptr) {
     a.q_norm = ea->q_norm;
@@ -1202,12 +1384,8 @@ int ov_gemm_f16_noalloc(const uint16_t* x, size_t ldx, const uint16_t* w, void* 
     NoAllocSetup(&scratch, &status);
     if (rows == 0) return;
     const int sms = SmCount();
-    const size_t need = GemmWorkspaceBytes(static_cast<int>(rows), static_cast<int>(out),
-                                           static_cast<int>(in), epilogue, sms);
-    if (need > kNoAllocScratchBytes)
-      throw Error(OV_ERR_INVALID, "needs " + std::to_string(need) +
-                                      " bytes of split-K scratch, more than the " +
-                                      std::to_string(kNoAllocScratchBytes) + "-byte static array");
+    // A product whose preferred split-K form needs more than the static
+    // array is planned as if it had no workspace (PlanGemm).
     GemmPlan plan;
     PlanGemm(&plan, x, static_cast<int64_t>(ldx), w, static_cast<int64_t>(out), 0, y,
              static_cast<int64_t>(ldy), static_cast<int>(rows), static_cast<int>(out),

@@ -28,9 +28,12 @@ struct GemmArgs {
   // after splits 0..s-1 did, so the sum order is fixed.
   uint32_t* counters = nullptr;
   // 1: the splits of a tile run as one thread-block cluster (one unit per
-  // CTA, split = rank in the cluster) and add their partials in split order
-  // through distributed shared memory; no counters.
+  // CTA, split = rank in the cluster); rank r sums column slice r of the
+  // splits' partials in split order.  The partials travel through `xchg`
+  // (global memory, [tile][sender][slice][128 x BN / splits floats]) when
+  // it is set, else through distributed shared memory; no counters.
   int cluster = 0;
+  float* xchg = nullptr;
   // OV_EPI_QKNORM_ROPE_F16
   const float* q_norm = nullptr;
   const float* k_norm = nullptr;
@@ -62,6 +65,7 @@ struct GemmShapeChoice {
   int splits;
   bool cluster = false;  // splits reduced inside a thread-block cluster
   bool pair = false;     // 256-row tiles on CTA pairs (cta_group::2 MMAs)
+  bool xchg = false;     // cluster splits exchange partials through the workspace
 };
 
 // Tile width and split-K factor for a product of this shape on `sms` SMs.
@@ -69,7 +73,9 @@ struct GemmShapeChoice {
 // split-K) or <bn>p1 (CTA pairs) in the environment overrides the choice
 // (tuning aid; ignored when the override is not valid for the product).
 GemmShapeChoice ChooseGemmShape(int M, int N, int K, int epilogue, bool have_workspace, int sms);
-// Workspace bytes a plan with this shape needs for split-K (0 if none).
+// Workspace bytes a plan with this shape needs for split-K (0 if none):
+// the order counters of serialised split-K or the partial slices of
+// cluster split-K.
 size_t GemmWorkspaceBytes(int M, int N, int K, int epilogue, int sms);
 
 // Builds a plan.  `w_rows` is the number of rows of the (possibly stacked)

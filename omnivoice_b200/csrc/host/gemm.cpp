@@ -27,7 +27,7 @@ bool Aligned(const void* p, std::size_t bytes) {
 
 struct HalfGemm::State {
   ov_stream_t stream = nullptr;
-  void* workspace = nullptr;  // split-K order counters, grow-only, zeroed
+  void* workspace = nullptr;  // split-K counters or partials, grow-only, zeroed
   std::size_t workspace_bytes = 0;
   ~State() {
     if (workspace != nullptr) ov_free(workspace);

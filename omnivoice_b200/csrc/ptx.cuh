@@ -61,6 +61,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
+// try_wait with acquire at cluster scope: what cluster peers wrote before
+// their release arrivals on `bar` (global memory included) is visible to
+// this thread once the phase completes.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
 // Non-blocking test of the phase with `parity` (for polling several
 // barriers from one thread).
 __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
@@ -82,6 +97,20 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
   const uint64_t start = global_timer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
+    if (global_timer_ns() - start > kWaitLimitNs) {
+      if (err != nullptr) atomicOr(err, kErrWaitTimeout);
+      return false;
+    }
+  }
+}
+
+// mbar_wait with cluster-scope acquire (mbar_try_wait_cluster); bounded the
+// same way.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, uint32_t* err) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t start = global_timer_ns();
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
     if (global_timer_ns() - start > kWaitLimitNs) {
       if (err != nullptr) atomicOr(err, kErrWaitTimeout);
       return false;
@@ -341,6 +370,16 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
                "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// The two halves of cluster_sync, for a barrier whose arrival happens long
+// before the wait (every thread of the cluster calls both, in this order).
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 // Shared::cluster address of the shared-memory byte at `smem_addr` (a

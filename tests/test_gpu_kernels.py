@@ -220,7 +220,10 @@ def test_gemm_every_tile_shape(monkeypatch, tile, epi):
     """Each compiled tile width, serialised split-K factor (<bn>x<splits>,
     residual add only), cluster split-K factor (<bn>c<splits>) and the
     CTA-pair kernel (256p1), forced through OV_GEMM_TILE, against float64
-    on ragged M and N."""
+    on ragged M and N.  Cluster split-K runs in both of its forms: partials
+    through distributed shared memory (a workspace too small for them) and
+    through global memory (a workspace of ov_gemm_workspace_bytes); both
+    sum in split order, so where both forms exist they agree bit for bit."""
     if epi == N.OV_EPI_STORE_F32 and "x" in tile and not tile.endswith("x1"):
         pytest.skip("serialised split-K applies to the residual epilogue only")
     monkeypatch.setenv("OV_GEMM_TILE", tile)
@@ -229,19 +232,31 @@ def test_gemm_every_tile_shape(monkeypatch, tile, epi):
     x = torch.randn(M, K, generator=g).half().cuda()
     w = (torch.randn(N_, K, generator=g) * 0.02).half().cuda()
     base = torch.randn(M, N_, generator=g).cuda()
-    ws = torch.zeros(4096, dtype=torch.uint8, device="cuda")
-    outs = []
-    for _ in range(2):
+
+    def run(ws):
         y = base.clone()
         gemm(x, w, y, epi, workspace=ws)
-        outs.append(y)
+        return y
+
+    small = torch.zeros(4096, dtype=torch.uint8, device="cuda")
+    outs = [run(small), run(small)]
+    if "c" in tile:
+        need = N.lib().ov_gemm_workspace_bytes(M, K, N_, epi)
+        assert need > 4096
+        big = torch.full((need,), 0xFF, dtype=torch.uint8, device="cuda")
+        outs += [run(big), run(big)]
     torch.cuda.synchronize()
     ref = x.double() @ w.double().T
     if epi == N.OV_EPI_ACCUM_F32:
         ref = ref + base.double()
     bound = K * 2.0 ** -23 * (x.double().abs() @ w.double().abs().T) + 1e-5 * base.double().abs() + 1e-6
-    assert ((outs[0].double() - ref).abs() <= bound).all()
+    for y in outs:
+        assert ((y.double() - ref).abs() <= bound).all()
     assert torch.equal(outs[0], outs[1])
+    if "c" in tile:
+        assert torch.equal(outs[2], outs[3])
+        if tile != "256c8":  # its slices do not fit the operand ring twice: no shared-memory form
+            assert torch.equal(outs[0], outs[2])
 
 
 @pytest.mark.parametrize("tile", [None, "256x1", "256p1"])
