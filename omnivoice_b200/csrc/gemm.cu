@@ -22,9 +22,12 @@
 //               bulk reduce-add into y (one writer per element: exact and
 //               deterministic).  The epilogue of unit i overlaps the MMAs
 //               of unit i+1 (double-buffered accumulators).
-// Split-K (residual epilogue, short M): the splits of a tile add their
-// partial sums into y in split order, ordered by a per-tile counter, so the
-// sum order is fixed.
+// Split-K (short M), always summed in split order so results do not depend
+// on timing: the splits of a tile run as one thread-block cluster and
+// exchange column slices of their partials (through the caller's workspace
+// in global memory, or else through distributed shared memory); or, for
+// the residual epilogue, they add into y one after another behind a
+// per-tile order counter.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
