@@ -164,26 +164,29 @@ __device__ __forceinline__ void SoftmaxRole(const AttnArgs& args, const CUtensor
     __syncwarp();  // the tensor-memory accesses below are warp-collective
     tc_fence_after_sync();
     const int valid = min(kKeys, len - t * kKeys);
-    // Pass 1: row maximum, 64 columns in registers at a time, the higher
-    // half first; keys past the sequence end read as -inf.  The lower half
-    // (columns col0 .. col0 + 63) stays in registers for pass 2: P is
-    // written over S columns k / 2, so S columns 32 .. 63 are overwritten
-    // (by this warpgroup in a tile pair, by the other warpgroup of a split
-    // tile once both passed the exchange barrier) and are never read again.
+    // Pass 1: row maximum over this warpgroup's key columns, all held in
+    // registers (one tensor-memory round trip per tile) for pass 2; keys
+    // past the sequence end read as -inf.  P is written over S columns
+    // k / 2 (by this warpgroup in a tile pair, by the other warpgroups of a
+    // split tile once all passed the exchange barrier), so no S column is
+    // read after it.
     float mt = -INFINITY;
     uint32_t ka[32], kb[kChunks >= 2 ? 32 : 1];
-    if (halves == 2) {
-      uint32_t ra[32], rb[32];
-      tmem_ld_32x32b_x32(s_addr + col0 + 64, ra);
-      tmem_ld_32x32b_x32(s_addr + col0 + 96, rb);
+    uint32_t kc[halves == 2 ? 32 : 1], kd[halves == 2 ? 32 : 1];
+    if constexpr (halves == 2) {
+      tmem_ld_32x32b_x32(s_addr + col0, ka);
+      tmem_ld_32x32b_x32(s_addr + col0 + 32, kb);
+      tmem_ld_32x32b_x32(s_addr + col0 + 64, kc);
+      tmem_ld_32x32b_x32(s_addr + col0 + 96, kd);
       tmem_ld_wait();
       if (valid < kKeys) {
-        mask_keys(ra, col0 + 64, valid);
-        mask_keys(rb, col0 + 96, valid);
+        mask_keys(ka, col0, valid);
+        mask_keys(kb, col0 + 32, valid);
+        mask_keys(kc, col0 + 64, valid);
+        mask_keys(kd, col0 + 96, valid);
       }
-      mt = fmaxf(max32(ra), max32(rb));
-    }
-    if constexpr (kChunks >= 2) {
+      mt = fmaxf(fmaxf(max32(ka), max32(kb)), fmaxf(max32(kc), max32(kd)));
+    } else if constexpr (kChunks >= 2) {
       tmem_ld_32x32b_x32(s_addr + col0, ka);
       tmem_ld_32x32b_x32(s_addr + col0 + 32, kb);
       tmem_ld_wait();
@@ -207,45 +210,28 @@ __device__ __forceinline__ void SoftmaxRole(const AttnArgs& args, const CUtensor
       for (int q = 1; q < kParts; ++q) mt = fmaxf(mt, xm[q * 128 + row]);
     }
     mt *= args.scale_log2;
+    // tcgen05.ld / st are warp-collective (.sync.aligned): the whole warp
+    // rescales when any of its rows needs it; rows whose maximum did not
+    // grow past the threshold keep theirs (alpha = 1).  Both warpgroups of
+    // a split tile see the same maxima, so they decide alike and each
+    // rescales its own O columns.  The rescale of O runs after this tile's
+    // probabilities are written (the scores' registers are free then) and
+    // before P V(t) is signalled.
+    bool rescale = false;
+    float alpha = 1.0f;
     if (t == 0) {
       m = mt;
     } else {
-      // tcgen05.ld / st are warp-collective (.sync.aligned): the whole
-      // warp rescales when any of its rows needs it; rows whose maximum
-      // did not grow past the threshold keep theirs (alpha = 1).  Both
-      // warpgroups of a split tile see the same maxima, so they decide
-      // alike and each rescales its own O columns.
       const bool grow = mt > m + kRescaleThreshold;
-      if (__any_sync(0xFFFFFFFFu, grow)) {
-        // Two tiles: the previous P V of this tile completed before S_t was
-        // written (one thread issues both, in order), so O is stable here.
-        // Split: S(t) may have run before P V(t - 1); wait for it.
-        if (split) {
-          (void)mbar_wait(pv_done, static_cast<uint32_t>(t - 1) & 1u, args.err);
-          __syncwarp();
-          tc_fence_after_sync();
-        }
+      rescale = __any_sync(0xFFFFFFFFu, grow);
+      if (rescale) {
         const float m_new = grow ? mt : m;
-        const float alpha = ex2_approx(m - m_new);
-        l *= alpha;
-#pragma unroll
-        for (int c = 0; c < kChunks; ++c) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(o_addr + col0 + c * 32, r);
-          tmem_ld_wait();
-#pragma unroll
-          for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * alpha);
-          tmem_st_32x32b_x16(o_addr + col0 + c * 32,
-                             *reinterpret_cast<const uint32_t(*)[16]>(&r[0]));
-          tmem_st_32x32b_x16(o_addr + col0 + c * 32 + 16,
-                             *reinterpret_cast<const uint32_t(*)[16]>(&r[16]));
-        }
+        alpha = ex2_approx(m - m_new);
         m = m_new;
       }
     }
     // Pass 2: probabilities, written as half pairs over the consumed S
-    // columns (key k -> column k / 2): the lower half from registers, then
-    // (tile pairs) the higher half, reloaded.
+    // columns (key k -> column k / 2).
     float rowsum = 0.0f;
     const float neg_m = -m;
     if constexpr (kChunks >= 2) {
@@ -259,20 +245,34 @@ __device__ __forceinline__ void SoftmaxRole(const AttnArgs& args, const CUtensor
       rowsum += probs32(ka, args.scale_log2, neg_m, pa);
       tmem_st_32x32b_x16(s_addr + col0 / 2, pa);
     }
-    if (halves == 2) {
-      uint32_t ra[32], rb[32];
-      tmem_ld_32x32b_x32(s_addr + col0 + 64, ra);
-      tmem_ld_32x32b_x32(s_addr + col0 + 96, rb);
-      tmem_ld_wait();
-      if (valid < kKeys) {
-        mask_keys(ra, col0 + 64, valid);
-        mask_keys(rb, col0 + 96, valid);
-      }
+    if constexpr (halves == 2) {
       uint32_t pa[16], pb[16];
-      rowsum += probs32(ra, args.scale_log2, neg_m, pa);
-      rowsum += probs32(rb, args.scale_log2, neg_m, pb);
+      rowsum += probs32(kc, args.scale_log2, neg_m, pa);
+      rowsum += probs32(kd, args.scale_log2, neg_m, pb);
       tmem_st_32x32b_x16(s_addr + col0 / 2 + 32, pa);
       tmem_st_32x32b_x16(s_addr + col0 / 2 + 48, pb);
+    }
+    if (rescale) {
+      // Two tiles: the previous P V of this tile completed before S_t was
+      // written (one thread issues both, in order), so O is stable here.
+      // Split: S(t) may have run before P V(t - 1); wait for it.
+      if (split) {
+        (void)mbar_wait(pv_done, static_cast<uint32_t>(t - 1) & 1u, args.err);
+        __syncwarp();
+        tc_fence_after_sync();
+      }
+      l *= alpha;
+#pragma unroll
+      for (int c = 0; c < kChunks; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(o_addr + col0 + c * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * alpha);
+        tmem_st_32x32b_x16(o_addr + col0 + c * 32, *reinterpret_cast<const uint32_t(*)[16]>(&r[0]));
+        tmem_st_32x32b_x16(o_addr + col0 + c * 32 + 16,
+                           *reinterpret_cast<const uint32_t(*)[16]>(&r[16]));
+      }
     }
     l += rowsum;
     tmem_st_wait();
