@@ -163,6 +163,8 @@ __device__ __forceinline__ void SoftmaxRole(const AttnArgs& args, const CUtensor
     (void)mbar_wait(&s_full[sb], sphase, args.err);
     __syncwarp();  // the tensor-memory accesses below are warp-collective
     tc_fence_after_sync();
+    if (threadIdx.x == 0 && t == 1) OV_ATRACE(3);
+    if (threadIdx.x == 0 && t == 2) OV_ATRACE(5);
     const int valid = min(kKeys, len - t * kKeys);
     // Pass 1: row maximum over this warpgroup's key columns, all held in
     // registers (one tensor-memory round trip per tile) for pass 2; keys
@@ -278,8 +280,7 @@ __device__ __forceinline__ void SoftmaxRole(const AttnArgs& args, const CUtensor
     tmem_st_wait();
     tc_fence_before_sync();
     mbar_arrive(&p_full[sb]);
-    if (threadIdx.x == 0 && t == 0) OV_ATRACE(3);
-    if (threadIdx.x == 0 && t == nt - 1) OV_ATRACE(4);
+    if (threadIdx.x == 0 && t == 1) OV_ATRACE(4);
   }
   if (split) {  // row sum = the sum of the parts, in part order
     xsum[wg * 128 + row] = l;
@@ -291,7 +292,6 @@ __device__ __forceinline__ void SoftmaxRole(const AttnArgs& args, const CUtensor
   (void)mbar_wait(&o_done[g], 0, args.err);
   __syncwarp();
   {
-    if (threadIdx.x == 0) OV_ATRACE(5);
     tc_fence_after_sync();
     const float inv = 1.0f / l;
     const int tile_row0 = q0 + g * kQ;
