@@ -86,6 +86,18 @@ class CodecConfigC(Structure):
                 ("upsampling_ratios", c_size_t * 8), ("num_upsampling", c_size_t),
                 ("sample_rate", c_uint32)]
 
+class CodecEncoderConfigC(Structure):
+    """ov_codec_encoder_config (include/ov_codec.h)."""
+    _fields_ = [("sample_rate", c_uint32), ("codebooks", c_size_t), ("codebook_size", c_size_t),
+                ("codebook_dim", c_size_t), ("semantic_sample_rate", c_uint32),
+                ("hidden_size", c_size_t), ("intermediate_size", c_size_t), ("heads", c_size_t),
+                ("layers", c_size_t), ("position_kernel", c_size_t), ("position_groups", c_size_t),
+                ("layer_norm_eps", c_float), ("conv_channels", c_size_t * 8),
+                ("conv_kernels", c_size_t * 8), ("conv_strides", c_size_t * 8),
+                ("num_convs", c_size_t), ("encoder_channels", c_size_t),
+                ("latent_channels", c_size_t), ("downsampling_ratios", c_size_t * 8),
+                ("num_downsampling", c_size_t)]
+
 
 CANCEL_FN = ctypes.CFUNCTYPE(c_int, c_void_p)
 
@@ -171,6 +183,14 @@ SIGNATURES: dict[str, tuple] = {
     "ov_codec_frame_samples": (c_size_t, [_P]),
     "ov_codec_decode": (c_int, [_P, _P, _S, _P]),
     "ov_codec_decode_device": (c_int, [_P, _P, _S, _P, _P]),
+    "ov_codec_encoder_default_config": (None, [POINTER(CodecEncoderConfigC)]),
+    "ov_codec_encoder_load": (c_int, [POINTER(CodecEncoderConfigC), c_char_p, c_int,
+                                      POINTER(c_void_p)]),
+    "ov_codec_encoder_create_synthetic": (c_int, [POINTER(CodecEncoderConfigC), c_uint64, c_int,
+                                                  POINTER(c_void_p)]),
+    "ov_codec_encoder_free": (None, [_P]),
+    "ov_codec_encoder_frame_samples": (c_size_t, [_P]),
+    "ov_codec_encode": (c_int, [_P, _P, _S, _P, _S, POINTER(c_size_t)]),
 }
 
 _lib: ctypes.CDLL | None = None
