@@ -1,7 +1,8 @@
 """Throughput of OmniVoice's generator hot path on B200.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload c2|c1|c3|c5|c4|codec|longtext] [--noise device|reference]
+                  [--workload c2|c1|c3|c5|c4|codec|encode|longtext]
+                  [--noise device|reference]
 
 A "step" is one full 32-step CFG unmasking generation of the workload.
 The default workload is BASELINE config 2 (120 text tokens + 250 masked
@@ -10,7 +11,8 @@ replicated across ranks with no collective on the data path (weak
 scaling).  `--workload c4` runs the batched config (64 utterances,
 partitioned across ranks by longest-processing-time, strong scaling).
 `--workload codec` times the audio tokenizer's decoder instead (codes of a
-250-frame chunk to 24 kHz audio, replicas only); `--workload longtext` a
+250-frame chunk to 24 kHz audio, replicas only); `--workload encode` the
+encoder (a 6 s reference voice to codes, replicas only); `--workload longtext` a
 60 s text as four chunks, generated (chunk 0, then chunks 1-3 batched) and
 decoded, beside the reference's chunk-by-chunk order.
 
@@ -511,6 +513,131 @@ def run_codec(args, rank, world):
         print(json.dumps(line), flush=True)
 
 
+ENCODE_SECONDS = 6.0       # config 3's voice-clone prompt: a 6 s reference (150 frames)
+
+
+def encoder_flops(cfg, samples: int) -> float:
+    """Multiply-add FLOPs of one encode (codec_encoder.cpp:249-458) of
+    `samples` 24 kHz samples with EncoderConfig `cfg`."""
+    flops = 0.0
+    n = int(np.ceil(samples * cfg.semantic_sample_rate / cfg.sample_rate)) + 320
+    cin = 1
+    for ch, k, st in zip(cfg.conv_channels, cfg.conv_kernels, cfg.conv_strides):
+        n = (n - k) // st + 1
+        flops += 2.0 * n * ch * cin * k
+        cin = ch
+    steps, h, i = n, cfg.hidden_size, cfg.intermediate_size
+    flops += 2.0 * steps * cin * h + 2.0 * steps * h * (h // cfg.position_groups) * cfg.position_kernel
+    flops += cfg.layers * (2.0 * steps * (4 * h * h + 2 * h * i) + 4.0 * steps * steps * h)
+    frames = samples // cfg.frame_samples
+    flops += 2.0 * frames * h * h * 25                     # semantic encoder: 25 taps of h x h
+    t, ch = samples, cfg.encoder_channels
+    flops += 2.0 * t * ch * 7
+    for s in cfg.downsampling_ratios:
+        flops += 3 * 2.0 * t * ch * ch * 8 + 2.0 * (t // s) * 2 * ch * ch * 2 * s
+        t, ch = t // s, 2 * ch
+    joint = h + cfg.latent_channels
+    flops += 2.0 * frames * cfg.latent_channels * ch * 3 + 2.0 * frames * joint * joint
+    flops += frames * cfg.codebooks * 4.0 * cfg.codebook_size * cfg.codebook_dim
+    return flops
+
+
+def run_encode(args, rank, world):
+    """--workload encode: the audio tokenizer's encoder (voice cloning: a
+    24 kHz reference to codes) on a 6 s reference; replicas only.  The
+    encode is host-driven like the reference's (resampling on the host, then
+    the device stages, codes back): value is the wall-clock rate of
+    ov_codec_encode with host samples and host codes (so e2e is the same
+    call), max over ranks."""
+    import torch
+
+    from omnivoice_b200.codec import Encoder, EncoderConfig
+    cfg = EncoderConfig()
+    enc = Encoder.synthetic(cfg, seed=1)
+    n = int(ENCODE_SECONDS * cfg.sample_rate)
+    samples = (0.3 * np.random.default_rng(rank).standard_normal(n)).astype(np.float32)
+    for _ in range(max(3, args.warmup)):
+        codes = enc.encode(samples)
+    torch.cuda.synchronize()
+    with ClockSampler(os.environ.get("CUDA_VISIBLE_DEVICES", "0").split(",")[0]) as clocks:
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            codes = enc.encode(samples)
+        sec = (time.perf_counter() - t0) / args.steps
+    assert codes.shape == (cfg.codebooks, n // cfg.frame_samples)
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([sec], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        sec = float(t.item())
+    flops = encoder_flops(cfg, n)
+    fp32_peak = 148 * 128 * 2 * 1.965e9 / 1e12
+    line = {
+        "metric": "reference-audio sec encoded per sec (codec encoder, 6 s reference)",
+        "value": world * ENCODE_SECONDS / sec, "unit": "audio_s/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic samples, random-init encoder weights",
+        "config": {"workload": f"codec encode of {n} samples ({ENCODE_SECONDS:g} s at 24 kHz) -> "
+                               f"8 x {n // cfg.frame_samples} codes",
+                   "parallelism": f"replicas{world}", "timing": "host wall clock per call"},
+        "roofline": {"bound": "fp32 (CUDA cores)", "achieved": flops / sec / 1e12, "peak": fp32_peak,
+                     "unit": "TFLOP/s", "frac": flops / sec / 1e12 / fp32_peak, "traffic": None,
+                     "note": "whole encode including host resampling and copies; peak nominal "
+                             "(148 SMs x 128 fp32 lanes x 2 x 1.965 GHz), no measured fp32 peak"},
+        "e2e": {"value": world * ENCODE_SECONDS / sec, "unit": "audio_s/s",
+                "h2d_bytes_per_step": int(samples.nbytes + 4 * int(np.ceil(n * 2 / 3 + 320))),
+                "d2h_bytes_per_step": int(codes.nbytes)},
+        "gpu_launches": args.steps * (len(cfg.conv_kernels) + 5 + 8 * cfg.layers + 1 + 11 +
+                                      2 + 7 * len(cfg.downsampling_ratios) + 2),
+        "clocks": clocks.summary(),
+    }
+    if not args.no_cpu_baseline:
+        from oracle import codec_encoder as oe
+        shape = oe.EncoderShape()
+        weights = oe.synthetic_weights(shape, 1)
+        sample = samples[:cfg.sample_rate]
+        t0 = time.perf_counter()
+        oe.encode(weights, shape, sample)
+        dt = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": 1.0 / dt, "unit": "audio_s/s", "cores": os.cpu_count(),
+                                "kind": "port",
+                                "sample": "oracle/codec_encoder.py (numpy float64) encoding 1 s"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def run_encode_reference(args, rank):
+    """--impl reference --workload encode: the CPU restatement of the
+    reference encoder (oracle/codec_encoder.py, numpy; the reference's own
+    encoder is HIP code) on a bounded sample: `steps` encodes of 1 s of the
+    reference audio.  Rank 0 only."""
+    if rank != 0:
+        return
+    from oracle import codec_encoder as oe
+    shape = oe.EncoderShape()
+    weights = oe.synthetic_weights(shape, 1)
+    sample = (0.3 * np.random.default_rng(0).standard_normal(shape.sample_rate)).astype(np.float32)
+    for _ in range(min(args.warmup, 1)):
+        oe.encode(weights, shape, sample)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oe.encode(weights, shape, sample)
+    per_second = (time.perf_counter() - t0) / args.steps
+    value = 1.0 / per_second
+    print(json.dumps({
+        "impl": "reference", "metric": "reference-audio sec encoded per sec (codec encoder, 6 s reference)",
+        "value": value, "unit": "audio_s/s", "n_gpus": 0, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": per_second * ENCODE_SECONDS * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic samples, random-init encoder weights",
+        "config": {"workload": "codec encode of a 6 s reference, sampled as 1 s"},
+        "cpu_baseline": {"value": value, "unit": "audio_s/s", "cores": os.cpu_count(),
+                         "kind": "port", "sample": "1 s encodes"},
+        "e2e": {"value": value, "unit": "audio_s/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0}}), flush=True)
+
+
 LONGTEXT_CHUNKS = 4        # a 60 s text: four 15 s chunks (synthesizer.cpp:166-178 chunking)
 LONGTEXT_FRAMES = 375
 LONGTEXT_TEXT = 150
@@ -613,7 +740,8 @@ def main():
     parser.add_argument("--steps", type=int, default=20)
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    parser.add_argument("--workload", choices=["c1", "c2", "c3", "c4", "c5", "codec", "longtext"],
+    parser.add_argument("--workload", choices=["c1", "c2", "c3", "c4", "c5", "codec", "encode",
+                                               "longtext"],
                         default="c2")
     parser.add_argument("--noise", choices=["device", "reference"], default="device")
     parser.add_argument("--no-cpu-baseline", action="store_true")
@@ -645,6 +773,11 @@ def main():
                 run_codec_reference(args, rank)
             else:
                 run_codec(args, rank, world)
+        elif args.workload == "encode":
+            if args.impl == "reference":
+                run_encode_reference(args, rank)
+            else:
+                run_encode(args, rank, world)
         elif args.impl == "reference":
             run_reference(args, rank, world)
         else:

@@ -1,7 +1,9 @@
 // Drop-in for the reference's audio tokenizer class (codec.hpp:17-43): the
-// same class and signatures, with Load and Decode implemented on the B200
-// C-ABI (ov_codec.h).  Encode (voice cloning) is not part of this library:
-// it returns false with "OmniVoice encode: not available in this build".
+// same class and signatures, with Load, Decode and Encode implemented on the
+// B200 C-ABI (ov_codec.h).  Load also loads the encoder when the config
+// describes one (semantic.conv_channels set, as the reference's config
+// parser always does); without it Encode returns false with an
+// "OmniVoice encode: " message.
 #ifndef GUFO_MODELS_OMNIVOICE_CODEC_HPP_
 #define GUFO_MODELS_OMNIVOICE_CODEC_HPP_
 
@@ -16,8 +18,8 @@
 
 namespace gufo::models::omnivoice {
 
-/// The Higgs Audio v2 tokenizer's decoder on one B200: RVQ codes to 24 kHz
-/// audio.  Uses the GPU current at Load.  Not thread-safe.
+/// The Higgs Audio v2 tokenizer on one B200: RVQ codes to 24 kHz audio and
+/// back.  Uses the GPU current at Load.  Not thread-safe.
 class Codec {
  public:
   /// Reads model_root / "audio_tokenizer" / "model.safetensors" (float32,
@@ -34,7 +36,8 @@ class Codec {
   [[nodiscard]] bool Decode(const std::vector<std::int32_t>& codes, std::size_t frames,
                             std::vector<float>* audio, std::string* error = nullptr);
 
-  /// Not available in this build (always false).
+  /// `samples` at sample_rate, a whole number of frames; yields
+  /// [codebook][frame] codes and the frame count.
   [[nodiscard]] bool Encode(const std::vector<float>& samples, std::vector<std::int32_t>* codes,
                             std::size_t* frames, std::string* error = nullptr);
 

@@ -30,7 +30,18 @@ struct BackboneConfig {
 /// only the width, which with the acoustic latent width makes the RVQ's
 /// hidden size.
 struct SemanticEncoderConfig {
+  std::uint32_t sample_rate = 0;
+  std::size_t frame_samples = 0;
   std::size_t hidden_size = 0;
+  std::size_t intermediate_size = 0;
+  std::size_t heads = 0;
+  std::size_t layers = 0;
+  std::size_t position_kernel = 0;
+  std::size_t position_groups = 0;
+  float layer_norm_eps = 0.0F;
+  std::vector<std::size_t> conv_channels;
+  std::vector<std::size_t> conv_kernels;
+  std::vector<std::size_t> conv_strides;
 };
 
 /// config.hpp:45-52 (DAC encoder and decoder of the acoustic branch).

@@ -7,7 +7,8 @@
 // decodes the [8][frames] codes read from <codes.i32> with Codec::Decode and
 // writes the samples to <audio.f32> for the Python test to compare with the
 // oracle; checks in place the reference's error messages (code count, code
-// range, missing checkpoint) and that Encode reports it is not built.
+// range, missing checkpoint) and that Encode, with no encoder in the config,
+// reports it.
 // Prints "ok" and exits 0 when every check holds.
 #include <cstdint>
 #include <cstdio>

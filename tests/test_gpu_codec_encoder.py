@@ -90,3 +90,30 @@ def test_synthetic_encoder_produces_codes(cuda_device, native):
     assert codes.shape == (8, 50)
     assert (codes >= 0).all() and (codes < 1024).all()
     assert len(set(codes[0].tolist())) > 5
+
+
+def test_cpp_dropin_encode(cuda_device, native, tmp_path):
+    """tests/cpp/codec_encoder_dropin_test.cpp: the reference-facing C++ class
+    loads a checkpoint holding decoder and encoder tensors, Codec::Encode
+    gives the oracle's codes and Codec::Decode takes them back to audio."""
+    import subprocess
+
+    from oracle import codec as oc
+    exe = Path(__file__).resolve().parents[1] / "omnivoice_b200" / "_build" / "codec_encoder_dropin_test"
+    if not exe.exists():
+        pytest.skip("codec_encoder_dropin_test not built (python -m omnivoice_b200.build)")
+    shape = oe.EncoderShape(**SMALL)
+    weights = oc.synthetic_weights(oc.CodecShape(codebook_size=shape.codebook_size,
+                                                 codebook_dim=shape.codebook_dim,
+                                                 semantic_hidden=shape.hidden,
+                                                 latent_channels=shape.latent_channels), 4)
+    weights.update(oe.synthetic_weights(shape, 4))  # the quantizer's shared tensors: the encoder's
+    (tmp_path / "audio_tokenizer").mkdir()
+    write_safetensors(tmp_path / "audio_tokenizer" / "model.safetensors", weights)
+    samples = (0.3 * np.random.default_rng(4).standard_normal(960 * 30)).astype(np.float32)
+    samples.tofile(tmp_path / "samples.f32")
+    out = subprocess.run([str(exe), str(tmp_path), str(tmp_path / "samples.f32"), str(samples.size),
+                          str(tmp_path / "codes.i32")], capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0 and out.stdout.strip().endswith("ok"), out.stdout + out.stderr
+    got = np.fromfile(tmp_path / "codes.i32", np.int32).reshape(8, 30)
+    assert (got == oe.encode(weights, shape, samples)).mean() >= 0.99
