@@ -67,6 +67,12 @@ struct ConvArgs {
   const float* resid;  // [rows_out][ldr] added after the activation, or null (may be y)
   int64_t ldr;
   int rows_out, cin_g, cout_g, groups, taps, stride, dilation, pad, pre, act;
+  // Split-K: splits > 1 CTAs share each output tile, split s taking
+  // (tap, 16-channel chunk) steps [s * per_split, (s + 1) * per_split) and
+  // writing raw sums to partial[s][rows_out][groups * cout_g]; reduce_kernel
+  // adds the splits in order and applies the epilogue.
+  float* partial;
+  int splits, per_split;
 };
 
 constexpr int kTileM = 64, kTileN = 64, kTileK = 16;
@@ -76,7 +82,11 @@ constexpr int kTileM = 64, kTileN = 64, kTileK = 16;
 __global__ void __launch_bounds__(256) conv_kernel(const ConvArgs a) {
   __shared__ __align__(16) float xs[kTileK][kTileM + 4];
   __shared__ __align__(16) float ws[kTileK][kTileN + 4];
-  const int g = blockIdx.z;
+  const int g = blockIdx.z / a.splits;
+  const int split = blockIdx.z % a.splits;
+  const int kchunks = (a.cin_g + kTileK - 1) / kTileK;
+  const int it0 = split * a.per_split;
+  const int it1 = min(it0 + a.per_split, a.taps * kchunks);
   const int m0 = blockIdx.x * kTileM;
   const int n0 = blockIdx.y * kTileN;
   const int tx = threadIdx.x & 15;   // output columns n0 + 4 tx ..
@@ -86,9 +96,11 @@ __global__ void __launch_bounds__(256) conv_kernel(const ConvArgs a) {
   for (int i = 0; i < 4; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
-  for (int tap = 0; tap < a.taps; ++tap) {
+  for (int it = it0; it < it1; ++it) {
+    const int tap = it / kchunks;
+    const int k0 = (it % kchunks) * kTileK;
     const float* wt = a.w + (static_cast<int64_t>(g) * a.taps + tap) * a.cout_g * a.cin_g;
-    for (int k0 = 0; k0 < a.cin_g; k0 += kTileK) {
+    {
       for (int i = threadIdx.x; i < kTileM * kTileK; i += 256) {
         const int r = i >> 4, kk = i & 15;
         const int m = m0 + r, ch = k0 + kk;
@@ -138,12 +150,31 @@ __global__ void __launch_bounds__(256) conv_kernel(const ConvArgs a) {
       const int n = n0 + 4 * tx + j;
       if (n >= a.cout_g) continue;
       const int o = g * a.cout_g + n;
+      if (a.splits > 1) {
+        a.partial[(static_cast<int64_t>(split) * a.rows_out + m) * (a.groups * a.cout_g) + o] = acc[i][j];
+        continue;
+      }
       float v = acc[i][j] + (a.bias != nullptr ? a.bias[o] : 0.0f);
       if (a.act == kActGelu) v = gelu(v);
       if (a.resid != nullptr) v += a.resid[static_cast<int64_t>(m) * a.ldr + o];
       a.y[static_cast<int64_t>(m) * a.ldy + o] = v;
     }
   }
+}
+
+// The splits of conv_kernel summed in split order, then its epilogue.
+__global__ void reduce_kernel(const ConvArgs a) {
+  const int cout = a.groups * a.cout_g;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= static_cast<int64_t>(a.rows_out) * cout) return;
+  const int64_t m = i / cout;
+  const int o = static_cast<int>(i % cout);
+  float v = 0.0f;
+  for (int s = 0; s < a.splits; ++s) v += a.partial[s * static_cast<int64_t>(a.rows_out) * cout + i];
+  v += a.bias != nullptr ? a.bias[o] : 0.0f;
+  if (a.act == kActGelu) v = gelu(v);
+  if (a.resid != nullptr) v += a.resid[m * a.ldr + o];
+  a.y[m * a.ldy + o] = v;
 }
 
 // ------------------------------------------------------------- attention
@@ -400,6 +431,7 @@ class EncoderEngine {
   EncoderEngine(const ov_codec_encoder_config& cfg, int device) : cfg_(cfg), device_(device) {
     Check(cudaSetDevice(device_), "cudaSetDevice");
     Check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
+    sms_ = SmCount();
     CheckConfig();
   }
   ~EncoderEngine() {
@@ -458,6 +490,8 @@ class EncoderEngine {
   DeviceBuffer<float> proj_in_w_, proj_in_b_, codebooks_, norms_, tables_;
   // work buffers
   DeviceBuffer<float> buf_[6];
+  DeviceBuffer<float> partial_;  // split-K partial sums
+  int sms_ = 148;
   DeviceBuffer<int32_t> codes_;
 };
 
@@ -704,8 +738,28 @@ int EncoderEngine::Run(const Conv& c, const float* x, int64_t ldx, int rows_in, 
   a.pre = pre;
   a.act = act;
   if (a.rows_out <= 0) throw Error(OV_ERR_INVALID, "reference audio too short for a convolution");
-  const dim3 grid((a.rows_out + kTileM - 1) / kTileM, (a.cout_g + kTileN - 1) / kTileN, c.groups);
+  // Split-K when the output tiles alone leave SMs idle: about two CTAs per
+  // SM, each split at least 8 steps deep.
+  const int tiles = ((a.rows_out + kTileM - 1) / kTileM) * ((a.cout_g + kTileN - 1) / kTileN) * c.groups;
+  const int steps = c.taps * ((c.cin_g + kTileK - 1) / kTileK);
+  int splits = std::min({(2 * sms_ + tiles - 1) / tiles, steps / 8, 16});
+  splits = std::max(splits, 1);
+  a.per_split = (steps + splits - 1) / splits;
+  a.splits = (steps + a.per_split - 1) / a.per_split;
+  a.partial = nullptr;
+  if (a.splits > 1) {
+    const size_t n = static_cast<size_t>(a.splits) * a.rows_out * c.groups * c.cout_g;
+    (void)partial_.Reserve(n);
+    a.partial = partial_.get();
+  }
+  const dim3 grid((a.rows_out + kTileM - 1) / kTileM, (a.cout_g + kTileN - 1) / kTileN,
+                  c.groups * a.splits);
   Launch(conv_kernel, grid, dim3(256), 0, stream_, "encoder conv launch", a);
+  if (a.splits > 1) {
+    const int64_t n = static_cast<int64_t>(a.rows_out) * c.groups * c.cout_g;
+    Launch(reduce_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, stream_,
+           "encoder split-K reduce launch", a);
+  }
   return a.rows_out;
 }
 
