@@ -114,3 +114,20 @@ def test_rejects_partial_frames():
     cfg, weights, samples = small_case(0.2)
     with pytest.raises(ValueError, match="whole number of frames"):
         enc.encode(weights, cfg, samples[:-1])
+
+
+ENC_GOLDEN = Path(__file__).parent / "golden" / "codec_encoder_golden.json"
+
+
+@pytest.mark.parametrize("case", ["small", "mid"])
+def test_encode_matches_transformers_golden(case):
+    """Codes of transformers' HiggsAudioV2TokenizerModel.encode (float64, the
+    published implementation the reference ports) on the seeded weights,
+    stored by tests/golden/make_codec_encoder_golden.py: the restatement
+    reproduces them exactly."""
+    g = {c["name"]: c for c in json.loads(ENC_GOLDEN.read_text())["cases"]}[case]
+    cfg = enc.EncoderShape(**g["shape"])
+    weights = enc.synthetic_weights(cfg, g["weight_seed"])
+    n = int(g["seconds"] * cfg.sample_rate) // cfg.frame_samples * cfg.frame_samples
+    samples = (0.3 * np.random.default_rng(g["sample_seed"]).standard_normal(n)).astype(np.float32)
+    assert np.array_equal(enc.encode(weights, cfg, samples), np.array(g["codes"]))

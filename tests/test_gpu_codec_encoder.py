@@ -117,3 +117,21 @@ def test_cpp_dropin_encode(cuda_device, native, tmp_path):
     assert out.returncode == 0 and out.stdout.strip().endswith("ok"), out.stdout + out.stderr
     got = np.fromfile(tmp_path / "codes.i32", np.int32).reshape(8, 30)
     assert (got == oe.encode(weights, shape, samples)).mean() >= 0.99
+
+
+@pytest.mark.parametrize("case", ["small", "mid"])
+def test_encode_matches_transformers_golden(cuda_device, native, tmp_path, case):
+    """The CUDA encoder on the cases of tests/golden/codec_encoder_golden.json
+    (codes of transformers' HiggsAudioV2TokenizerModel.encode in float64)."""
+    import json
+    g = {c["name"]: c for c in json.loads((Path(__file__).parent / "golden" /
+                                           "codec_encoder_golden.json").read_text())["cases"]}[case]
+    shape = oe.EncoderShape(**g["shape"])
+    weights = oe.synthetic_weights(shape, g["weight_seed"])
+    write_safetensors(tmp_path / "w.safetensors", weights)
+    enc = Encoder.load(config_of(shape), str(tmp_path / "w.safetensors"))
+    n = int(g["seconds"] * shape.sample_rate) // shape.frame_samples * shape.frame_samples
+    samples = (0.3 * np.random.default_rng(g["sample_seed"]).standard_normal(n)).astype(np.float32)
+    got = enc.encode(samples)
+    enc.close()
+    assert (got == np.array(g["codes"])).mean() >= 0.99
