@@ -115,7 +115,8 @@ __device__ unsigned long long g_attn_trace[4096 * 8];
 struct AttnArgs {
   const int32_t* cu_seqlens;
   // [n][2] work items (sequence, first 128-query tile | max groups << 24),
-  // or null: sequence blockIdx.y, tiles 2 blockIdx.x and 2 blockIdx.x + 1.
+  // one per blockIdx.y with the head in blockIdx.x; or null: sequence
+  // blockIdx.y, tiles 2 blockIdx.x and 2 blockIdx.x + 1, head blockIdx.z.
   const int32_t* items;
   __half* out;
   int64_t ld_out;
@@ -367,8 +368,10 @@ __global__ void __launch_bounds__(ThreadsOf(kWG), 1)
   pdl_trigger();
   int seq, tile, max_groups;
   if (args.items != nullptr) {
-    seq = args.items[2 * blockIdx.x];
-    const int code = args.items[2 * blockIdx.x + 1];
+    // Work items: head blockIdx.x, item blockIdx.y, so the hardware starts
+    // the items (longest first) in order across all heads.
+    seq = args.items[2 * blockIdx.y];
+    const int code = args.items[2 * blockIdx.y + 1];
     tile = code & 0xFFFFFF;
     max_groups = code >> 24;
   } else if (args.single) {
@@ -381,7 +384,7 @@ __global__ void __launch_bounds__(ThreadsOf(kWG), 1)
     max_groups = 2;
   }
   if (kWG == 4) max_groups = 1;  // the four-warpgroup form takes single tiles only
-  const int h = blockIdx.z;
+  const int h = args.items != nullptr ? static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.z);
   const int start = args.cu_seqlens[seq];
   const int len = args.cu_seqlens[seq + 1] - start;
   const int q0 = tile * kQ;
@@ -657,8 +660,10 @@ void LaunchAttention(const CUtensorMap& map_qkv, const CUtensorMap& map_out,
   a.err = DeviceErrorWord();
   a.single = single ? 1 : 0;
   const int per = single ? kQ : 2 * kQ;
+  if (items != nullptr && n_items > 65535)
+    throw Error(OV_ERR_UNSUPPORTED, "more than 65535 attention work items");
   const dim3 grid = items != nullptr
-                        ? dim3(static_cast<unsigned>(n_items), 1, static_cast<unsigned>(heads))
+                        ? dim3(static_cast<unsigned>(heads), static_cast<unsigned>(n_items), 1)
                         : dim3(static_cast<unsigned>((max_seqlen + per - 1) / per),
                                static_cast<unsigned>(num_seqs), static_cast<unsigned>(heads));
   if (single) {
