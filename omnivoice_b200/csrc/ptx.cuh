@@ -26,8 +26,6 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   return t;
 }
 
-__device__ __forceinline__ uint32_t elect_lane0() { return (threadIdx.x & 31u) == 0u; }
-
 // ------------------------------------------------------------- mbarriers
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
@@ -388,13 +386,6 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t smem_addr, uint32_t ran
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
   return r;
-}
-
-__device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
-                                              uint32_t d) {
-  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b),
-               "r"(c), "r"(d)
-               : "memory");
 }
 
 // Bulk copy of `bytes` (a multiple of 16) from this CTA's shared memory
