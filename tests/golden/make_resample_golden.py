@@ -3,8 +3,9 @@ fixture (tests/fixtures/audio_golden.json of the reference tree, made by
 torchaudio) into tests/golden/resample_golden.json: per case the signal
 spec, the rates, the output length and every `stride`-th output sample.
 
-Run from the repository root with the reference tree at REF (default
-/root/reference); the fixture is copied as data, no reference code runs."""
+Run from the repository root with the reference tree at $REF (or the
+default location in the code below); the fixture is copied as data, no
+reference code runs."""
 from __future__ import annotations
 
 import json
