@@ -33,6 +33,7 @@ enum {
 
 typedef void* ov_stream_t; /* a cudaStream_t; NULL is the legacy stream */
 typedef void* ov_event_t;  /* a cudaEvent_t */
+typedef void* ov_graph_t;  /* an instantiated cudaGraphExec_t */
 
 /* Copies the calling thread's last error message (NUL-terminated, truncated
  * to `capacity`) and returns the last status code.  Mirrors the
@@ -66,6 +67,16 @@ int ov_event_destroy(ov_event_t event);
 int ov_event_record(ov_event_t event, ov_stream_t stream);
 int ov_event_sync(ov_event_t event);
 int ov_event_elapsed_ms(ov_event_t begin, ov_event_t end, float* milliseconds);
+
+/* CUDA graphs (no counterpart in the reference, which launches every
+ * kernel each step): ov_graph_capture_begin starts a thread-local capture
+ * of `stream` (which must not be the legacy stream); ov_graph_capture_end
+ * ends it and instantiates the captured work as *graph; ov_graph_launch
+ * replays it on `stream`. */
+int ov_graph_capture_begin(ov_stream_t stream);
+int ov_graph_capture_end(ov_stream_t stream, ov_graph_t* graph);
+int ov_graph_launch(ov_graph_t graph, ov_stream_t stream);
+int ov_graph_destroy(ov_graph_t graph);
 
 /* Device-side error word written by kernels whose bounded waits ran out
  * (no kernel of this library traps).  Reads and clears it on `device`'s

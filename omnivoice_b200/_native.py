@@ -128,6 +128,10 @@ SIGNATURES: dict[str, tuple] = {
     "ov_event_record": (c_int, [_P, _P]),
     "ov_event_sync": (c_int, [_P]),
     "ov_event_elapsed_ms": (c_int, [_P, _P, POINTER(c_float)]),
+    "ov_graph_capture_begin": (c_int, [_P]),
+    "ov_graph_capture_end": (c_int, [_P, POINTER(c_void_p)]),
+    "ov_graph_launch": (c_int, [_P, _P]),
+    "ov_graph_destroy": (c_int, [_P]),
     "ov_take_device_errors": (c_int, [POINTER(c_uint32), _P]),
     # ov_kernels.h
     "ov_embed": (c_int, [_P, _S, _P, _P, _S, _P, _S, _S, _S, _P, _P, c_float, _P, _P]),

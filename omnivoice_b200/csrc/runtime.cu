@@ -246,6 +246,39 @@ int ov_event_elapsed_ms(ov_event_t begin, ov_event_t end, float* milliseconds) {
   return e == cudaSuccess ? OV_OK : CudaFail(e, "cudaEventElapsedTime");
 }
 
+int ov_graph_capture_begin(ov_stream_t stream) {
+  if (stream == nullptr) return ovb::Guard("ov_graph_capture_begin: ", [] {
+      throw ovb::Error(OV_ERR_INVALID, "the legacy stream cannot be captured");
+    });
+  const cudaError_t e =
+      cudaStreamBeginCapture(AsStream(stream), cudaStreamCaptureModeThreadLocal);
+  return e == cudaSuccess ? OV_OK : CudaFail(e, "cudaStreamBeginCapture");
+}
+
+int ov_graph_capture_end(ov_stream_t stream, ov_graph_t* graph) {
+  *graph = nullptr;
+  cudaGraph_t g = nullptr;
+  cudaError_t e = cudaStreamEndCapture(AsStream(stream), &g);
+  if (e != cudaSuccess) return CudaFail(e, "cudaStreamEndCapture");
+  cudaGraphExec_t exec = nullptr;
+  e = cudaGraphInstantiate(&exec, g, 0);
+  (void)cudaGraphDestroy(g);
+  if (e != cudaSuccess) return CudaFail(e, "cudaGraphInstantiate");
+  *graph = exec;
+  return OV_OK;
+}
+
+int ov_graph_launch(ov_graph_t graph, ov_stream_t stream) {
+  const cudaError_t e = cudaGraphLaunch(reinterpret_cast<cudaGraphExec_t>(graph), AsStream(stream));
+  return e == cudaSuccess ? OV_OK : CudaFail(e, "cudaGraphLaunch");
+}
+
+int ov_graph_destroy(ov_graph_t graph) {
+  if (graph == nullptr) return OV_OK;
+  const cudaError_t e = cudaGraphExecDestroy(reinterpret_cast<cudaGraphExec_t>(graph));
+  return e == cudaSuccess ? OV_OK : CudaFail(e, "cudaGraphExecDestroy");
+}
+
 int ov_take_device_errors(uint32_t* flags, ov_stream_t stream) {
   return ovb::Guard("", [&] {
     uint32_t* word = ovb::DeviceErrorWord();

@@ -442,3 +442,31 @@ def test_select_device_noise_picks_only_masked_slots():
     changed = np.nonzero(got != codes)[0]
     assert (changed >= n // 2).all()
     assert ((got[n // 2:] != 1024).sum()) == 300
+
+
+# ---------------------------------------------------------------- runtime
+
+def test_graph_capture_replays_the_captured_copies():
+    """ov_graph_capture_begin / _end / ov_graph_launch (include/ov_runtime.h):
+    a memset and a device copy captured on a stream replay on every launch;
+    the legacy stream is refused."""
+    lib = N.lib()
+    s = ctypes.c_void_p()
+    ok(lib.ov_stream_create(ctypes.byref(s)))
+    src = torch.arange(4096, dtype=torch.float32, device="cuda")
+    dst = torch.zeros(4096, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    ok(lib.ov_graph_capture_begin(s))
+    ok(lib.ov_memset_async(p(dst), 0, dst.numel() * 4, s))
+    ok(lib.ov_memcpy_d2d_async(p(dst), p(src), 2048 * 4, s))
+    graph = ctypes.c_void_p()
+    ok(lib.ov_graph_capture_end(s, ctypes.byref(graph)))
+    for _ in range(2):
+        dst.fill_(-1.0)
+        torch.cuda.synchronize()
+        ok(lib.ov_graph_launch(graph, s))
+        ok(lib.ov_stream_sync(s))
+        assert torch.equal(dst[:2048], src[:2048]) and (dst[2048:] == 0).all()
+    ok(lib.ov_graph_destroy(graph))
+    ok(lib.ov_stream_destroy(s))
+    assert lib.ov_graph_capture_begin(None) == N.OV_ERR_INVALID
