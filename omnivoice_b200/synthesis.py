@@ -112,3 +112,63 @@ def synthesize_chunks_sequential(generator, codec, count: int,
 
 def chunk_seconds(results: Sequence[ChunkResult], frame_rate: float = 25.0) -> float:
     return sum(r.codes.shape[1] for r in results) / frame_rate
+
+
+@dataclass
+class ClonedVoice:
+    """A reference voice encoded for cloning (synthesizer.cpp:111-130's
+    ReferenceVoice): its codes [codebooks][frames] and transcript."""
+    codes: np.ndarray
+    text: str
+
+    @property
+    def frames(self) -> int:
+        return int(self.codes.shape[1])
+
+
+def clone_voice(encoder, samples, text: str) -> ClonedVoice:
+    """Synthesizer::CloneVoice's encode step (synthesizer.cpp:111-130): the
+    transcript is required and the prepared 24 kHz mono samples are encoded
+    by the codec encoder (`encoder.encode`, omnivoice_b200.codec.Encoder).
+    Preparing the recording (downmix, resampling to 24 kHz, level, silence
+    removal and the trim to whole frames, audio.cpp PrepareReference) is the
+    caller's; samples that are not a whole number of frames raise the
+    encoder's error."""
+    if not text.strip():
+        raise ValueError("OmniVoice: voice cloning needs the reference transcript")
+    return ClonedVoice(np.asarray(encoder.encode(samples)), text)
+
+
+def fingerprint(samples, text: str) -> int:
+    """64-bit FNV-1a over the samples' bytes and the transcript's, the key of
+    the runner's voice cache (runner.cpp:22-35)."""
+    h = 1469598103934665603
+    for data in (np.ascontiguousarray(samples, dtype=np.float32).tobytes(), text.encode()):
+        for b in data:
+            h = ((h ^ b) * 1099511628211) & 0xFFFFFFFFFFFFFFFF
+    return h
+
+
+class VoiceCache:
+    """The runner's cache of cloned voices (runner.cpp:143-172): the
+    `capacity` most recently used recordings and transcripts, each encoded
+    once; a hit moves to the front, the least recently used falls out."""
+
+    def __init__(self, encoder, capacity: int = 8):
+        self.encoder = encoder
+        self.capacity = capacity
+        self._entries: list[tuple[int, ClonedVoice]] = []  # most recent first
+
+    def __len__(self) -> int:
+        return len(self._entries)
+
+    def get(self, samples, text: str) -> ClonedVoice:
+        key = fingerprint(samples, text)
+        for i, (k, voice) in enumerate(self._entries):
+            if k == key:
+                self._entries.insert(0, self._entries.pop(i))
+                return voice
+        voice = clone_voice(self.encoder, samples, text)
+        self._entries.insert(0, (key, voice))
+        del self._entries[self.capacity:]
+        return voice

@@ -45,3 +45,49 @@ def test_batched_chunks_match_chunk_by_chunk(cuda_device, native, count, has_ref
         assert a.audio.shape == (frames[a.index] * 24,) and np.isfinite(a.audio).all()
     gen.close()
     codec.close()
+
+
+def test_cloned_voice_prompts_the_chunks(cuda_device, native, tmp_path):
+    """Voice cloning end to end: a recording encoded once by the CUDA codec
+    encoder through the runner's voice cache (its codes equal the encoder
+    oracle's), then used as the caller's reference voice for every chunk."""
+    import sys
+    from pathlib import Path
+    sys.path.insert(0, str(Path(__file__).parent))
+    from model_files import write_safetensors
+    from omnivoice_b200.codec import Encoder, EncoderConfig
+    from omnivoice_b200.synthesis import VoiceCache
+    from oracle import codec_encoder as oe
+
+    shape = oe.EncoderShape(codebook_size=64, codebook_dim=8, hidden=32, intermediate=64, heads=4,
+                            layers=2, position_kernel=16, position_groups=4,
+                            conv_channels=[16, 16, 16, 16], conv_kernels=[10, 4, 4, 4],
+                            conv_strides=[5, 4, 4, 4], encoder_channels=4, latent_channels=32)
+    weights = oe.synthetic_weights(shape, 6)
+    write_safetensors(tmp_path / "enc.safetensors", weights)
+    enc = Encoder.load(EncoderConfig(codebook_size=64, codebook_dim=8, hidden_size=32,
+                                     intermediate_size=64, heads=4, layers=2, position_kernel=16,
+                                     position_groups=4, conv_channels=[16, 16, 16, 16],
+                                     conv_kernels=[10, 4, 4, 4], conv_strides=[5, 4, 4, 4],
+                                     encoder_channels=4, latent_channels=32),
+                       str(tmp_path / "enc.safetensors"))
+    recording = (0.3 * np.random.default_rng(6).standard_normal(960 * 20)).astype(np.float32)
+    cache = VoiceCache(enc)
+    voice = cache.get(recording, "a reference transcript")
+    assert cache.get(recording, "a reference transcript") is voice and len(cache) == 1
+    assert np.array_equal(voice.codes, oe.encode(weights, shape, recording))
+    enc.close()
+
+    cfg = small_config()
+    gen = Generator.synthetic(cfg, weight_seed=6)
+    rng = np.random.default_rng(7)
+    texts = [rng.integers(0, cfg.vocab_size, 10).tolist() for _ in range(3)]
+
+    def build(i, carried):
+        assert carried is None  # the caller's voice: no carry-over
+        return ConditionalInput.build(texts[i], voice.codes, 24)
+
+    out = synthesize_chunks(gen, None, 3, build, DecodingConfig(steps=8), seed=3, has_reference=True)
+    gen.close()
+    assert [r.codes.shape for r in out] == [(8, 24)] * 3
+    assert all(((r.codes >= 0) & (r.codes < 1024)).all() for r in out)

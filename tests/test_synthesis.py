@@ -8,6 +8,7 @@ from dataclasses import dataclass
 import numpy as np
 import pytest
 
+from omnivoice_b200 import synthesis
 from omnivoice_b200.synthesis import (synthesize_chunks, synthesize_chunks_sequential)
 
 
@@ -97,3 +98,53 @@ def test_batch_override_and_errors():
     with pytest.raises(RuntimeError, match="results"):
         synthesize_chunks(None, None, 3, builder([4, 4, 4]), None, seed=0,
                           batch=lambda inputs, d, s: [])
+
+
+# ------------------------------------------------------------ voice cloning
+
+class CountingEncoder:
+    """Stands in for omnivoice_b200.codec.Encoder: codes from the samples'
+    mean, and a count of the encodes."""
+
+    def __init__(self):
+        self.calls = 0
+
+    def encode(self, samples):
+        self.calls += 1
+        samples = np.asarray(samples, np.float32)
+        if samples.size == 0 or samples.size % 960:
+            raise ValueError("OmniVoice encode: reference audio must be a whole number of frames")
+        frames = samples.size // 960
+        return np.full((8, frames), int(abs(samples.mean()) * 1000) % 1024, np.int32)
+
+
+def test_clone_voice_needs_a_transcript_and_encodes_once():
+    enc = CountingEncoder()
+    with pytest.raises(ValueError, match="needs the reference transcript"):
+        synthesis.clone_voice(enc, np.zeros(960, np.float32), "  ")
+    voice = synthesis.clone_voice(enc, np.full(960 * 3, 0.25, np.float32), "hello")
+    assert voice.frames == 3 and voice.text == "hello" and enc.calls == 1
+
+
+def test_fingerprint_is_fnv1a_over_samples_and_text():
+    # FNV-1a 64 of the empty input is the offset basis; one byte moves it.
+    assert synthesis.fingerprint(np.zeros(0, np.float32), "") == 1469598103934665603
+    a = synthesis.fingerprint(np.zeros(4, np.float32), "x")
+    assert a != synthesis.fingerprint(np.zeros(4, np.float32), "y")
+    assert a == synthesis.fingerprint(np.zeros(4, np.float32), "x")
+
+
+def test_voice_cache_encodes_each_recording_once_and_evicts_lru():
+    enc = CountingEncoder()
+    cache = synthesis.VoiceCache(enc, capacity=2)
+    rec = [np.full(960, v, np.float32) for v in (0.1, 0.2, 0.3)]
+    cache.get(rec[0], "a")
+    cache.get(rec[1], "b")
+    cache.get(rec[0], "a")          # hit, moves to the front
+    assert enc.calls == 2
+    cache.get(rec[2], "c")          # evicts rec[1] (least recently used)
+    assert len(cache) == 2
+    cache.get(rec[0], "a")
+    assert enc.calls == 3
+    cache.get(rec[1], "b")          # evicted: encoded again
+    assert enc.calls == 4
