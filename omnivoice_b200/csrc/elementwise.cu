@@ -78,22 +78,46 @@ __global__ void __launch_bounds__(kRowsPerBlock * 32)
   } else {
 #pragma unroll
     for (int i = 0; i < kVec; ++i) x[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int c = 0; c < codebooks; ++c) {
+    // The codes first (independent loads), then each codebook's row loaded
+    // while the previous one is added; the sum runs in codebook order.
+    auto row_of = [&](int c) {
       int64_t code = ids[static_cast<int64_t>(c) * rows + row];
       if (code < 0 || code >= audio_vocab) {
         if (lane == 0) atomicOr(err, kErrBadArgument);
         code = 0;
       }
-      const float* src = audio_table + (static_cast<int64_t>(c) * audio_vocab + code) * width;
+      return audio_table + (static_cast<int64_t>(c) * audio_vocab + code) * width;
+    };
+    constexpr int kPrefetch = 8;
+    const float* srcs[kPrefetch];
+#pragma unroll
+    for (int c = 0; c < kPrefetch; ++c) srcs[c] = c < codebooks ? row_of(c) : nullptr;
+    float4 cur[kVec], next[kVec];
+    if (codebooks > 0) {
+#pragma unroll
+      for (int i = 0; i < kVec; ++i) cur[i] = *reinterpret_cast<const float4*>(srcs[0] + (i * 32 + lane) * 4);
+    }
+    auto step = [&](int c, const float* next_src) {
+      if (next_src != nullptr) {
+#pragma unroll
+        for (int i = 0; i < kVec; ++i)
+          next[i] = *reinterpret_cast<const float4*>(next_src + (i * 32 + lane) * 4);
+      }
 #pragma unroll
       for (int i = 0; i < kVec; ++i) {
-        const float4 v = *reinterpret_cast<const float4*>(src + (i * 32 + lane) * 4);
-        x[i].x += v.x;
-        x[i].y += v.y;
-        x[i].z += v.z;
-        x[i].w += v.w;
+        x[i].x += cur[i].x;
+        x[i].y += cur[i].y;
+        x[i].z += cur[i].z;
+        x[i].w += cur[i].w;
+        cur[i] = next[i];
       }
+    };
+#pragma unroll
+    for (int c = 0; c < kPrefetch; ++c) {
+      if (c >= codebooks) break;
+      step(c, c + 1 >= codebooks ? nullptr : c + 1 < kPrefetch ? srcs[c + 1] : row_of(c + 1));
     }
+    for (int c = kPrefetch; c < codebooks; ++c) step(c, c + 1 < codebooks ? row_of(c + 1) : nullptr);
   }
   float* dst = hidden + row * width;
 #pragma unroll
