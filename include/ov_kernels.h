@@ -143,9 +143,10 @@ int ov_interleave_gate_up(const uint16_t* gate_up, size_t width, size_t in, uint
  *   - The first call on a device sets up that device (looks up the array's
  *     device address with that device current and clears its counters);
  *     make that first call before any stream capture.
- *   - Products whose preferred split-K form needs more than 64 KiB of
- *     scratch (cluster split-K exchanging its partials through global
- *     memory) run as ov_gemm_f16 would without a workspace.
+ *   - Split-K here uses the scratch only for its per-tile order counters
+ *     (the partial-slice exchange of ov_gemm_f16's workspace is not
+ *     offered); a product that would need more than 64 KiB of counters is
+ *     rejected with OV_ERR_INVALID (none does on a 148-SM B200).
  *   - Every call shares the array, which keeps the last call's contents:
  *     calls that overlap on the GPU (different streams, or different host
  *     threads on one device) race and must be serialised by the caller. */

@@ -39,6 +39,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <string>
 
 #include "gemm.hpp"
 #include "internal.hpp"
@@ -1053,7 +1054,8 @@ int ClusterCapacity(int splits, int sms) {
 
 }  // namespace
 
-GemmShapeChoice ChooseGemmShape(int M, int N, int K, int epilogue, bool have_workspace, int sms) {
+GemmShapeChoice ChooseGemmShape(int M, int N, int K, int epilogue, bool have_workspace, int sms,
+                                bool allow_xchg) {
   if (const char* env = std::getenv("OV_GEMM_TILE")) {
     int bn = 0, splits = 1;
     char sep = 'x';
@@ -1061,9 +1063,11 @@ GemmShapeChoice ChooseGemmShape(int M, int N, int K, int epilogue, bool have_wor
       const bool cluster = sep == 'c';
       if (sep == 'p') {
         if (ValidPairShape(bn, N, epilogue)) return {bn, 1, false, true};
-      } else if (ValidShape(bn, splits, cluster, N, K, epilogue, cluster && have_workspace) &&
+      } else if (ValidShape(bn, splits, cluster, N, K, epilogue,
+                            cluster && have_workspace && allow_xchg) &&
                  (splits == 1 || cluster || have_workspace)) {
-        return {bn, splits, cluster && splits > 1, false, cluster && splits > 1 && have_workspace};
+        return {bn, splits, cluster && splits > 1, false,
+                cluster && splits > 1 && have_workspace && allow_xchg};
       }
     }
   }
@@ -1086,7 +1090,7 @@ GemmShapeChoice ChooseGemmShape(int M, int N, int K, int epilogue, bool have_wor
       for (int cl = 0; cl < 2; ++cl) {
         const bool cluster = cl == 1;
         if (cluster && s == 1) continue;
-        const bool xchg = cluster && have_workspace;
+        const bool xchg = cluster && have_workspace && allow_xchg;
         if (!ValidShape(bn, s, cluster, N, K, epilogue, xchg)) continue;
         if (s > 1 && !cluster && (!have_workspace || s > 4)) continue;
         const double units = static_cast<double>(Tiles(M, N, bn)) * s;
@@ -1134,7 +1138,7 @@ size_t GemmWorkspaceBytes(int M, int N, int K, int epilogue, int sms) {
 void PlanGemm(GemmPlan* plan, const uint16_t* x, int64_t ldx, const uint16_t* w, int64_t w_rows,
               int b_row_offset, void* y, int64_t ldy, int M, int N, int K, int epilogue,
               const ov_epilogue_args* ea, void* workspace, size_t workspace_bytes, int sms,
-              uint32_t* err) {
+              uint32_t* err, bool allow_xchg) {
   OV_REQUIRE(M > 0 && N > 0 && K > 0, "empty GEMM");
   OV_REQUIRE(K % kBK == 0, "GEMM K must be a multiple of 64");
   OV_REQUIRE(ldx % 8 == 0 && ldx >= K, "x row stride must be a multiple of 8 and >= K");
@@ -1145,10 +1149,10 @@ void PlanGemm(GemmPlan* plan, const uint16_t* x, int64_t ldx, const uint16_t* w,
   // A workspace too small (or, for the partial slices, not 16-byte
   // aligned) for the chosen split-K form: choose again without one.
   const bool ws_ok = workspace != nullptr && workspace_bytes > 0;
-  GemmShapeChoice choice = ChooseGemmShape(M, N, K, epilogue, ws_ok, sms);
+  GemmShapeChoice choice = ChooseGemmShape(M, N, K, epilogue, ws_ok, sms, allow_xchg);
   if (workspace_bytes < WorkspaceNeed(M, N, choice) ||
       (choice.xchg && (reinterpret_cast<uintptr_t>(workspace) & 15u) != 0))
-    choice = ChooseGemmShape(M, N, K, epilogue, false, sms);
+    choice = ChooseGemmShape(M, N, K, epilogue, false, sms, allow_xchg);
   int out_cols = N;
   if (epilogue == OV_EPI_SWIGLU_F16) {
     OV_REQUIRE(N % 128 == 0, "SwiGLU output features must be a multiple of 128");
@@ -1387,12 +1391,22 @@ int ov_gemm_f16_noalloc(const uint16_t* x, size_t ldx, const uint16_t* w, void* 
     NoAllocSetup(&scratch, &status);
     if (rows == 0) return;
     const int sms = SmCount();
-    // A product whose preferred split-K form needs more than the static
-    // array is planned as if it had no workspace (PlanGemm).
+    // The static array holds split-K order counters only (one per output
+    // tile of the serialised form); the partial-slice exchange, whose
+    // workspace grows with the product, is not offered here.
+    const size_t need = WorkspaceNeed(
+        static_cast<int>(rows), static_cast<int>(out),
+        ChooseGemmShape(static_cast<int>(rows), static_cast<int>(out), static_cast<int>(in),
+                        epilogue, true, sms, /*allow_xchg=*/false));
+    if (need > kNoAllocScratchBytes)
+      throw Error(OV_ERR_INVALID, "needs " + std::to_string(need) +
+                                      " bytes of split-K scratch, more than the " +
+                                      std::to_string(kNoAllocScratchBytes) + "-byte static array");
     GemmPlan plan;
     PlanGemm(&plan, x, static_cast<int64_t>(ldx), w, static_cast<int64_t>(out), 0, y,
              static_cast<int64_t>(ldy), static_cast<int>(rows), static_cast<int>(out),
-             static_cast<int>(in), epilogue, args, scratch, kNoAllocScratchBytes, sms, status);
+             static_cast<int>(in), epilogue, args, scratch, kNoAllocScratchBytes, sms, status,
+             /*allow_xchg=*/false);
     switch (InstanceKey(plan.bn, plan.epilogue, plan.pair)) {
 #define OV_DIRECT_CASE(BN, EPI, PAIR) \
   case InstanceKey(BN, EPI, PAIR): LaunchTyped<BN, EPI, PAIR>(plan, AsStream(stream)); break;

@@ -72,7 +72,10 @@ struct GemmShapeChoice {
 // OV_GEMM_TILE=<bn>x<splits> (serialised split-K), <bn>c<splits> (cluster
 // split-K) or <bn>p1 (CTA pairs) in the environment overrides the choice
 // (tuning aid; ignored when the override is not valid for the product).
-GemmShapeChoice ChooseGemmShape(int M, int N, int K, int epilogue, bool have_workspace, int sms);
+// allow_xchg false: with a workspace, only its order-counter use (serialised
+// split-K) is considered, never the partial-slice exchange.
+GemmShapeChoice ChooseGemmShape(int M, int N, int K, int epilogue, bool have_workspace, int sms,
+                                bool allow_xchg = true);
 // Workspace bytes a plan with this shape needs for split-K (0 if none):
 // the order counters of serialised split-K or the partial slices of
 // cluster split-K.
@@ -85,7 +88,7 @@ size_t GemmWorkspaceBytes(int M, int N, int K, int epilogue, int sms);
 void PlanGemm(GemmPlan* plan, const uint16_t* x, int64_t ldx, const uint16_t* w, int64_t w_rows,
               int b_row_offset, void* y, int64_t ldy, int M, int N, int K, int epilogue,
               const ov_epilogue_args* epilogue_args, void* workspace, size_t workspace_bytes,
-              int sms, uint32_t* err = nullptr);
+              int sms, uint32_t* err = nullptr, bool allow_xchg = true);
 
 void LaunchGemm(const GemmPlan& plan, cudaStream_t stream);
 
