@@ -65,7 +65,7 @@ typedef struct {
   const int32_t* ids;
 } ov_conditional_input;
 
-/* Noise of the position choice (decoding.cpp:221-227):
+/* Noise of the position choice (decoding.cpp:82-87):
  *   OV_GEN_NOISE_REFERENCE - the reference's own stream: std::mt19937_64(seed),
  *     one draw per [codebook][frame] slot per non-empty step, u = (x >> 40) * 2^-24,
  *     Gumbel -log(-log(u + 1e-10) + 1e-10), drawn on the host and uploaded once;

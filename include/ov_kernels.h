@@ -138,15 +138,20 @@ int ov_interleave_gate_up(const uint16_t* gate_up, size_t width, size_t in, uint
  * This entry point allocates nothing.  Its split-K scratch (per-tile order
  * counters) is a 64 KiB file-scope device array that every GPU loading the
  * library holds until the process exits; bounded waits report into a status
- * word kept with it.
+ * word kept with it, which ov_take_device_errors reads and clears together
+ * with the library's other device error word.
  * Inputs and outputs are the caller's, as for ov_gemm_f16.
  *   - The first call on a device sets up that device (looks up the array's
- *     device address with that device current and clears its counters);
+ *     device address with that device current, clears it and the status
+ *     word, and measures the cluster capacities the tile choice uses);
  *     make that first call before any stream capture.
  *   - Split-K here uses the scratch only for its per-tile order counters
  *     (the partial-slice exchange of ov_gemm_f16's workspace is not
  *     offered); a product that would need more than 64 KiB of counters is
- *     rejected with OV_ERR_INVALID (none does on a 148-SM B200).
+ *     rejected with OV_ERR_INVALID (none does on a 148-SM B200).  A call
+ *     that uses them clears them first (cudaMemsetAsync on `stream`), so a
+ *     split whose wait timed out in an earlier call leaves no stale order
+ *     behind.
  *   - Every call shares the array, which keeps the last call's contents:
  *     calls that overlap on the GPU (different streams, or different host
  *     threads on one device) race and must be serialised by the caller. */
@@ -198,7 +203,7 @@ int ov_score(const float* logits, size_t ld, size_t frames, size_t codebooks, si
              uint32_t mask_id, float guidance, int32_t* prediction, float* confidence,
              ov_stream_t stream);
 
-/* Noise sources of the position choice (decoding.cpp:221-227). */
+/* Noise sources of the position choice (decoding.cpp:82-87). */
 enum {
   OV_NOISE_NONE = 0,    /* temperature 0: greedy position choice            */
   OV_NOISE_DEVICE = 1,  /* counter-based Philox-4x32-10 on the device       */
@@ -206,7 +211,7 @@ enum {
                            std::mt19937_64 stream of the reference          */
 };
 
-/* decoding.cpp:211-248 (PositionSelector::Fill) plus the code write-back of
+/* decoding.cpp:70-106 (PositionSelector::Fill) plus the code write-back of
  * generator.cpp:526-535, on the device, for one utterance:
  *   score = confidence - c * layer_penalty;  if temperature > 0:
  *   score = score / temperature + gumbel;  slots whose code is not mask_id
@@ -224,7 +229,7 @@ int ov_select_positions(const int32_t* prediction, const float* confidence, size
                         ov_stream_t stream);
 
 /* Host helper: the Gumbel value the device path derives from a uniform u,
- * -log(-log(u + 1e-10) + 1e-10) in float32 (decoding.cpp:225-226). */
+ * -log(-log(u + 1e-10) + 1e-10) in float32 (decoding.cpp:84-85). */
 float ov_gumbel_from_uniform(float uniform);
 
 /* -------------------------------------------------- synthetic weights */

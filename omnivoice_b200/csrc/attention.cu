@@ -99,18 +99,6 @@ __device__ __forceinline__ float probs32(const uint32_t (&r)[32], float scale, f
   return a + b;
 }
 
-#ifdef OV_ATTN_TRACE
-// Timing probe of a diagnostic build: %globaltimer at milestones per CTA
-// (compiled only with -DOV_ATTN_TRACE).
-__device__ unsigned long long g_attn_trace[4096 * 8];
-#define OV_ATRACE(slot)                                                          \
-  g_attn_trace[(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z)) % 4096 * 8 + \
-               (slot)] = global_timer_ns()
-#else
-#define OV_ATRACE(slot) \
-  do {                  \
-  } while (0)
-#endif
 
 struct AttnArgs {
   const int32_t* cu_seqlens;
@@ -164,8 +152,6 @@ __device__ __forceinline__ void SoftmaxRole(const AttnArgs& args, const CUtensor
     (void)mbar_wait(&s_full[sb], sphase, args.err);
     __syncwarp();  // the tensor-memory accesses below are warp-collective
     tc_fence_after_sync();
-    if (threadIdx.x == 0 && t == 1) OV_ATRACE(3);
-    if (threadIdx.x == 0 && t == 2) OV_ATRACE(5);
     const int valid = min(kKeys, len - t * kKeys);
     // Pass 1: row maximum over this warpgroup's key columns, all held in
     // registers (one tensor-memory round trip per tile) for pass 2; keys
@@ -281,7 +267,6 @@ __device__ __forceinline__ void SoftmaxRole(const AttnArgs& args, const CUtensor
     tmem_st_wait();
     tc_fence_before_sync();
     mbar_arrive(&p_full[sb]);
-    if (threadIdx.x == 0 && t == 1) OV_ATRACE(4);
   }
   if (split) {  // row sum = the sum of the parts, in part order
     xsum[wg * 128 + row] = l;
@@ -361,7 +346,6 @@ __global__ void __launch_bounds__(ThreadsOf(kWG), 1)
                      const __grid_constant__ CUtensorMap map_out, const AttnArgs args) {
   constexpr int kProducerWarp = 4 * kWG;
   constexpr int kMmaWarp = 4 * kWG + 1;
-  if (threadIdx.x == 0) OV_ATRACE(0);
   // The next kernel may start its prologue now; this one waits for its
   // inputs (q, k, v of the previous kernel) only after its own set-up.  The
   // work items and sequence bounds are uploaded before the step.
@@ -444,7 +428,6 @@ __global__ void __launch_bounds__(ThreadsOf(kWG), 1)
   tc_fence_after_sync();
   const uint32_t tmem = *tmem_slot;
   pdl_wait();  // q, k, v of the previous kernel are complete
-  if (threadIdx.x == 0) OV_ATRACE(1);
 
   if (warp == kProducerWarp) {
     // Lane 0 loads Q and the K tiles, lane 1 the V tiles, each into a
@@ -510,7 +493,6 @@ __global__ void __launch_bounds__(ThreadsOf(kWG), 1)
                       (t > 0 || kk > 0) ? 1u : 0u);
       };
       bool ok = mbar_wait(q_full, 0, args.err) && mbar_wait(&k_full[0], 0, args.err);
-      OV_ATRACE(2);
       if (ok && groups == 1) {
         // One query tile: S alternates between the two S/P regions, so
         // S(t + 1) runs on the tensor core while the softmax turns S(t)
@@ -620,14 +602,6 @@ __global__ void __launch_bounds__(ThreadsOf(kWG), 1)
   if (warp == kMmaWarp) {
     tc_fence_after_sync();
     tmem_dealloc(tmem, 512);
-#ifdef OV_ATTN_TRACE
-    if (lane == 0) {
-      OV_ATRACE(6);
-      uint32_t smid;
-      asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
-      g_attn_trace[(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z)) % 4096 * 8 + 7] = smid;
-    }
-#endif
   }
 }
 
@@ -697,18 +671,6 @@ void EncodeQkvMap(CUtensorMap* map, const uint16_t* qkv, int64_t ld_qkv, int64_t
 
 using namespace ovb;
 
-#ifdef OV_ATTN_TRACE
-extern "C" int ov_debug_attn_trace(unsigned long long* out, size_t count, int clear) {
-  if (clear) {
-    static unsigned long long zeros[4096 * 8];
-    return cudaMemcpyToSymbol(ovb::g_attn_trace, zeros, sizeof(zeros)) == cudaSuccess ? 0 : 2;
-  }
-  return cudaMemcpyFromSymbol(out, ovb::g_attn_trace, count * sizeof(unsigned long long)) ==
-                 cudaSuccess
-             ? 0
-             : 2;
-}
-#endif
 
 extern "C" int ov_attention_varlen(const uint16_t* qkv, size_t ld_qkv, size_t rows,
                                    const int32_t* cu_seqlens, size_t num_seqs,

@@ -1,6 +1,6 @@
 // The decoding tail of one unmasking step on the device:
 //   score_kernel  - guided log-softmax scoring, generator_kernels.hip:212-265
-//   select_kernel - PositionSelector::Fill (decoding.cpp:211-248) and the
+//   select_kernel - PositionSelector::Fill (decoding.cpp:70-106) and the
 //                   code write-back of generator.cpp:526-535.
 // Both read per-utterance descriptors so one launch serves a packed batch.
 #include <cuda_runtime.h>

@@ -471,16 +471,6 @@ __device__ __forceinline__ void ClusterReduce(const GemmArgs& a, const CUtensorM
   }
 }
 
-#ifdef OV_GEMM_TRACE
-// Timing probe of a diagnostic build: %globaltimer at pipeline milestones
-// per CTA (compiled only with -DOV_GEMM_TRACE).
-__device__ unsigned long long g_gemm_trace[1024 * 16];
-#define OV_TRACE(slot) g_gemm_trace[blockIdx.x * 16 + (slot)] = global_timer_ns()
-#else
-#define OV_TRACE(slot) \
-  do {                 \
-  } while (0)
-#endif
 
 // Cluster split-K through global memory (args.xchg set): each rank writes
 // the other ranks' column slices of its partial to the workspace, then
@@ -605,9 +595,7 @@ __device__ __forceinline__ void XchgSplitK(const GemmArgs& a, const CUtensorMap*
     }
     (void)mbar_wait_cluster(inbox_bar, 0, a.err);
     __syncwarp();
-    if (c.ep == 0) OV_TRACE(14);
     XchgReduce<BN, EPI, S>(a, map_y, c, tacc, tile, m_tile, n_tile, rank);
-    if (c.ep == 0) OV_TRACE(15);
   }
 }
 
@@ -640,7 +628,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) OV_TRACE(0);
   // The next kernel may start its prologue (its CTAs find SMs only as this
   // grid's leave); every read of this kernel's inputs waits below.
   pdl_trigger();
@@ -689,7 +676,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   // wait half runs after the MMAs, by when every rank has long arrived.
   if (kClusterSplit && args.xchg != nullptr) cluster_arrive();
   const uint32_t tmem = *tmem_slot;
-  if (threadIdx.x == 0) OV_TRACE(1);
   if (!(warp == 0 && lane == 0)) pdl_wait();  // inputs of the previous kernel are ready
 
   if (warp == 0) {
@@ -727,7 +713,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       pdl_wait();
-      OV_TRACE(2);
       uint32_t k_iter = 0;
       bool ok = true;
       for (int u = unit0; ok && u < args.units; u += ustep) {
@@ -754,7 +739,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                args.b_row_offset + n_tile * BN + static_cast<int>(rank) * b_rows);
         }
       }
-      OV_TRACE(10);
       // Let the copies this thread started land before the CTA can exit
       // (PAIR rank 1: its copies land on rank 0's barriers, which rank 0's
       // MMAs consume before this CTA's accumulators are complete).
@@ -799,7 +783,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          if (k_iter == 0) OV_TRACE(3);
           tc_fence_after_sync();
           const uint32_t a0 = smem_u32(sa + s * Cfg::kABytes);
           const uint32_t b0 = smem_u32(sb + s * Cfg::kBBytes);
@@ -822,9 +805,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_commit_pair(&tfull[buf], 0x3);
         else
           umma_commit(&tfull[buf]);
-        if (acc_iter == 0) OV_TRACE(4);
       }
-      OV_TRACE(11);
     }
     if (kClusterSplit && args.cluster) {
       __syncwarp();
@@ -862,7 +843,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       // (the error word is set) so the 256 threads stay in step.
       (void)mbar_wait(&tfull[buf], static_cast<uint32_t>(acc_iter >> 1) & 1u, args.err);
       __syncwarp();  // the tensor-memory loads below are warp-collective
-      if (acc_iter == 0 && c.ep == 0) OV_TRACE(5);
       tc_fence_after_sync();
       if (args.cluster) break;  // one unit per CTA, reduced below
       const int tile = u / args.splits;
@@ -870,7 +850,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Earlier splits of this tile first; their adds are complete.
         if (c.ep == 0) {
           (void)wait_counter_equals(args.counters + tile, static_cast<uint32_t>(split), args.err);
-          if (acc_iter == 0) OV_TRACE(12);
         }
         named_barrier(kEpiBarrier, 256);
         if (c.gep == 0) fence_proxy_async_global();
@@ -902,7 +881,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             red_release_gpu_add(args.counters + tile, 1u);
         }
       }
-      if (acc_iter == 0 && c.ep == 0) OV_TRACE(6);
     }
     if constexpr (kClusterSplit) {
       if (args.cluster) {
@@ -913,7 +891,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t tacc = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
         __syncwarp();
         if (args.xchg != nullptr) {
-          if (c.ep == 0) OV_TRACE(12);
           c.ring = smem;  // all MMAs are complete: the idle ring stages the stores
           const int tile = static_cast<int>(blockIdx.x) / args.splits;
           switch (args.splits) {
@@ -931,7 +908,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_before_sync();
           cluster_sync();
           tc_fence_after_sync();
-          if (c.ep == 0) OV_TRACE(12);
           if (c.ep == 0) {
             const uint32_t slot_bytes = static_cast<uint32_t>(kBM * (BN / args.splits) * 4);
             mbar_arrive_expect_tx(inbox_bar, static_cast<uint32_t>(args.splits - 1) * slot_bytes);
@@ -939,35 +915,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           ClusterSend<BN>(tacc, smem, c, split, args.splits, inbox_bar);
           (void)mbar_wait(inbox_bar, 0, args.err);
           __syncwarp();
-          if (c.ep == 0) OV_TRACE(14);
           ClusterReduce<BN, EPI>(args, &map_y, c, tacc, smem, m_tile, n_tile, split);
-          if (c.ep == 0) OV_TRACE(15);
           // No CTA leaves while a peer's bulk copy may still read its outbox.
           __syncwarp();
           cluster_sync();
         }
-        if (c.ep == 0) OV_TRACE(6);
       }
     }
     // Each group leader's stores have read their staging tiles before the
     // CTA's shared memory goes away; the writes complete with the grid.
     if (c.gep == 0) bulk_wait_group_read<0>();
-#ifdef OV_GEMM_TRACE
-    if (c.ep == 0) {
-      OV_TRACE(7);
-      uint32_t smid;
-      asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
-      g_gemm_trace[blockIdx.x * 16 + 9] = static_cast<unsigned long long>(acc_iter);
-      g_gemm_trace[blockIdx.x * 16 + 13] = smid;
-    }
-#endif
   }
   tc_fence_before_sync();
   if constexpr (PAIR)
     cluster_sync();  // no CTA leaves while its peer may still signal it
   else
     __syncthreads();
-  if (threadIdx.x == 0) OV_TRACE(8);
   if (warp == 1) {
     tc_fence_after_sync();
     if constexpr (PAIR)
@@ -1309,7 +1272,10 @@ uint8_t* g_noalloc_scratch_ptr[kNoAllocDevices] = {};
 uint32_t* g_noalloc_status_ptr[kNoAllocDevices] = {};
 
 // Once per device, with it current: device addresses of the static arrays,
-// cleared split-K counters, and the kernels' shared-memory limits.
+// cleared split-K counters and status word, the kernels' shared-memory
+// limits and the resident-cluster capacities the tile chooser reads (the
+// same set-up ov_gemm_f16's callers get, so both entry points choose the
+// same tiles).  None of it allocates device memory.
 void NoAllocSetup(uint8_t** scratch, uint32_t** status) {
   int device = 0;
   Check(cudaGetDevice(&device), "cudaGetDevice");
@@ -1329,6 +1295,7 @@ void NoAllocSetup(uint8_t** scratch, uint32_t** status) {
         "cudaFuncSetAttribute(max dynamic shared memory)");
     OV_GEMM_INSTANCES(OV_SET_DIRECT)
 #undef OV_SET_DIRECT
+    ConfigureGemmKernels();
     g_noalloc_status_ptr[device] = static_cast<uint32_t*>(tp);
     g_noalloc_scratch_ptr[device] = static_cast<uint8_t*>(sp);
   }
@@ -1337,6 +1304,17 @@ void NoAllocSetup(uint8_t** scratch, uint32_t** status) {
 }
 
 }  // namespace
+
+uint32_t* NoAllocStatusWord() {
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kNoAllocDevices) {
+    (void)cudaGetLastError();
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  return g_noalloc_status_ptr[device];
+}
+
 }  // namespace ovb
 
 using namespace ovb;
@@ -1407,6 +1385,12 @@ int ov_gemm_f16_noalloc(const uint16_t* x, size_t ldx, const uint16_t* w, void* 
              static_cast<int64_t>(ldy), static_cast<int>(rows), static_cast<int>(out),
              static_cast<int>(in), epilogue, args, scratch, kNoAllocScratchBytes, sms, status,
              /*allow_xchg=*/false);
+    // The order counters must start at zero.  The last split of each tile
+    // resets its counter, but a split whose wait timed out leaves it set,
+    // so every call clears the counters it uses, in stream order.
+    if (plan.args.counters != nullptr)
+      Check(cudaMemsetAsync(plan.args.counters, 0, need, AsStream(stream)),
+            "clear split-K counters");
     switch (InstanceKey(plan.bn, plan.epilogue, plan.pair)) {
 #define OV_DIRECT_CASE(BN, EPI, PAIR) \
   case InstanceKey(BN, EPI, PAIR): LaunchTyped<BN, EPI, PAIR>(plan, AsStream(stream)); break;
@@ -1419,16 +1403,3 @@ int ov_gemm_f16_noalloc(const uint16_t* x, size_t ldx, const uint16_t* w, void* 
 
 }  // extern "C"
 
-#ifdef OV_GEMM_TRACE
-extern "C" int ov_debug_gemm_trace_clear() {
-  static unsigned long long zeros[1024 * 16];
-  return cudaMemcpyToSymbol(ovb::g_gemm_trace, zeros, sizeof(zeros)) == cudaSuccess ? 0 : 2;
-}
-
-extern "C" int ov_debug_gemm_trace(unsigned long long* out, size_t count) {
-  return cudaMemcpyFromSymbol(out, ovb::g_gemm_trace, count * sizeof(unsigned long long)) ==
-                 cudaSuccess
-             ? 0
-             : 2;
-}
-#endif

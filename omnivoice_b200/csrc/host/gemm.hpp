@@ -1,4 +1,4 @@
-// Drop-in for the reference's HalfGemm (gemm.hpp:11-72): float16 products
+// Drop-in for the reference's HalfGemm (gemm.hpp:12-71): float16 products
 // with float32 accumulation and output.  Linear runs on the tcgen05 GEMM
 // (ov_gemm_f16) and Matmul on ov_matmul_f16; the hipBLASLt handle of the
 // reference's constructor becomes an unused pointer and its HIP stream an

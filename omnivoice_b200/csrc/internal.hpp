@@ -49,6 +49,10 @@ inline void CheckStatus(int status) {
 // The device error word of the current device (allocated on first use).
 uint32_t* DeviceErrorWord();
 
+// The status word of ov_gemm_f16_noalloc on the current device (a static
+// device array), or nullptr while that entry point has not run there.
+uint32_t* NoAllocStatusWord();
+
 // Streaming multiprocessors of the current device.
 int SmCount();
 

@@ -287,7 +287,18 @@ int ov_take_device_errors(uint32_t* flags, ov_stream_t stream) {
                "read device error word");
     ovb::Check(cudaMemsetAsync(word, 0, sizeof(uint32_t), AsStream(stream)),
                "clear device error word");
+    // The allocation-free GEMM reports into its own static word.
+    uint32_t noalloc = 0;
+    uint32_t* status = ovb::NoAllocStatusWord();
+    if (status != nullptr) {
+      ovb::Check(cudaMemcpyAsync(&noalloc, status, sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                                 AsStream(stream)),
+                 "read allocation-free GEMM status word");
+      ovb::Check(cudaMemsetAsync(status, 0, sizeof(uint32_t), AsStream(stream)),
+                 "clear allocation-free GEMM status word");
+    }
     ovb::Check(cudaStreamSynchronize(AsStream(stream)), "device error word");
+    *flags |= noalloc;
   });
 }
 

@@ -21,7 +21,7 @@ Text chunking, prompt building and tokenisation (synthesizer.cpp:166-178,
 prompt.cpp) stay with the caller: `build_input(index, voice)` returns the
 ConditionalInput of chunk `index` given the reference voice `voice` (None,
 or the carried Voice of chunk 0).  Cross-fading and post-processing of the
-pieces (synthesizer.cpp:208-212) are the caller's too.
+pieces (synthesizer.cpp:202-206) are the caller's too.
 """
 from __future__ import annotations
 

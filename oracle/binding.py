@@ -55,9 +55,29 @@ _oracle = None
 _ref = None
 
 
+def reference_tree() -> str | None:
+    """Where the reference sources are: $OV_REF_DIR, else the
+    `reference_path` that BASELINE.json at the repository root records;
+    None when neither names an existing directory."""
+    import json
+    import os
+    path = os.environ.get("OV_REF_DIR")
+    if not path:
+        baseline = HERE.parent / "BASELINE.json"
+        try:
+            path = json.loads(baseline.read_text()).get("reference_path")
+        except (OSError, ValueError):
+            path = None
+    return path if path and Path(path).is_dir() else None
+
+
 def build() -> None:
     """Builds liboracle.so (and oracle/_ref when the reference tree exists)."""
-    subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+    cmd = ["make", "-s", "-C", str(HERE)]
+    ref = reference_tree()
+    if ref is not None:
+        cmd.append(f"REF={ref}")
+    subprocess.run(cmd, check=True)
 
 
 def oracle() -> ctypes.CDLL:

@@ -459,7 +459,7 @@ void oc_build_input(const uint32_t* text_ids, size_t text_count, const int32_t* 
   }
 }
 
-// decoding.cpp:225-226: u = (x >> 40) * 2^-24, gumbel = -log(-log(u + 1e-10) + 1e-10).
+// decoding.cpp:84-85: u = (x >> 40) * 2^-24, gumbel = -log(-log(u + 1e-10) + 1e-10).
 void oc_reference_gumbel(uint64_t seed, size_t count, float* out) {
   std::mt19937_64 random(seed);
   for (size_t i = 0; i < count; ++i) {

@@ -85,7 +85,7 @@ void oc_build_input(const uint32_t* text_ids, size_t text_count, const int32_t* 
                     uint32_t mask_id, int32_t* ids_out);
 
 /* The first `count` Gumbel values of the reference's std::mt19937_64(seed)
- * noise stream (decoding.cpp:225-226). */
+ * noise stream (decoding.cpp:84-85). */
 void oc_reference_gumbel(uint64_t seed, size_t count, float* out);
 
 /* PositionSelector::Fill with the noise given as Gumbel values per slot

@@ -15,7 +15,9 @@ from pathlib import Path
 
 
 def main() -> None:
-    root = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) < 2:
+        sys.exit("usage: make_decoding_golden.py REFERENCE_ROOT")
+    root = Path(sys.argv[1])
     source = json.loads((root / "tests/fixtures/generator_golden.json").read_text())
     out = {"source": "reference tests/fixtures/generator_golden.json (decoding fields)",
            "config": source["config"], "generate": []}

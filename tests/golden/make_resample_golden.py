@@ -3,9 +3,8 @@ fixture (tests/fixtures/audio_golden.json of the reference tree, made by
 torchaudio) into tests/golden/resample_golden.json: per case the signal
 spec, the rates, the output length and every `stride`-th output sample.
 
-Run from the repository root with the reference tree at $REF (or the
-default location in the code below); the fixture is copied as data, no
-reference code runs."""
+Run from the repository root with the reference tree at $REF; the fixture
+is copied as data, no reference code runs."""
 from __future__ import annotations
 
 import json
@@ -13,10 +12,11 @@ import os
 import sys
 from pathlib import Path
 
-REF = Path(os.environ.get("REF", "/root/reference"))
-
 
 def main() -> None:
+    if not os.environ.get("REF"):
+        sys.exit("set REF to the reference tree")
+    REF = Path(os.environ["REF"])
     src = json.loads((REF / "tests" / "fixtures" / "audio_golden.json").read_text())
     cases = [{"signal": e["signal"], "target": e["target"], "length": e["length"],
               "samples": e["samples"]} for e in src["resample"]]

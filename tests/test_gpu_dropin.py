@@ -1,5 +1,5 @@
 """The C++ drop-in API (csrc/host/generator.hpp and gemm.hpp, the
-reference's generator.hpp:16-56 and gemm.hpp:11-72) on the B200.
+reference's generator.hpp:16-56 and gemm.hpp:12-71) on the B200.
 
 tests/cpp/dropin_test.cpp loads a model.safetensors through
 Generator::Load, runs Forward, Score, Generate and GenerateBatch, checks

@@ -28,10 +28,21 @@ def _ok(status):
         raise AssertionError(N.last_error())
 
 
-@pytest.mark.parametrize("M,N_,K,epi", [(240, 1024, 3072, N.OV_EPI_ACCUM_F32),
-                                        (620, 1024, 2048, N.OV_EPI_ACCUM_F32),
-                                        (500, 8200, 1024, N.OV_EPI_STORE_F32)])
-def test_noalloc_gemm_matches_allocating_entry_point(cuda_device, native, M, N_, K, epi):
+@pytest.mark.parametrize("M,N_,K,epi,tile", [(240, 1024, 3072, N.OV_EPI_ACCUM_F32, None),
+                                             (620, 1024, 2048, N.OV_EPI_ACCUM_F32, None),
+                                             (500, 8200, 1024, N.OV_EPI_STORE_F32, None),
+                                             (620, 1024, 3072, N.OV_EPI_ACCUM_F32, "128x4"),
+                                             (240, 1024, 2048, N.OV_EPI_ACCUM_F32, "64x2")])
+def test_noalloc_gemm_matches_allocating_entry_point(cuda_device, native, monkeypatch, M, N_, K,
+                                                     epi, tile):
+    if tile is not None:
+        # Serialised split-K (the tile chooser reads OV_GEMM_TILE on every
+        # call): the splits of a tile add into y in order behind a per-tile
+        # counter, and those counters are what the static array holds.
+        monkeypatch.setenv("OV_GEMM_TILE", tile)
+        bn, splits = map(int, tile.split("x"))
+        tiles = -(-M // 128) * -(-N_ // bn)
+        assert native.ov_gemm_workspace_bytes(M, K, N_, epi) == 4 * tiles
     stream = torch.cuda.current_stream().cuda_stream
     g = torch.Generator().manual_seed(M + K)
     x = torch.randn(M, K, generator=g).half().cuda()
@@ -46,13 +57,15 @@ def test_noalloc_gemm_matches_allocating_entry_point(cuda_device, native, M, N_,
     if epi == N.OV_EPI_ACCUM_F32:
         ref = ref + base.double()
     bound = K * 2.0 ** -23 * (x.double().abs() @ w.double().abs().T) + 1e-5 * base.double().abs() + 1e-6
-    for _ in range(2):  # two calls in a row share the static scratch
+    for _ in range(3):  # calls in a row share the static scratch
         got = base.clone()
         _ok(native.ov_gemm_f16_noalloc(x.data_ptr(), K, w.data_ptr(), got.data_ptr(), N_, M, K,
                                        N_, epi, None, stream))
         torch.cuda.synchronize()
         assert ((got.double() - ref).abs() <= bound).all()
         assert ((got.double() - want.double()).abs() <= bound).all()
+    # Reads (and clears) the library's error word and this entry point's
+    # own status word: no bounded wait of any call above ran out.
     flags = ctypes.c_uint32()
     _ok(native.ov_take_device_errors(ctypes.byref(flags), stream))
     assert flags.value == 0
