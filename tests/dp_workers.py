@@ -42,33 +42,45 @@ def _init(rank, world, port, timeout_s):
 
 
 def worker(rank, world, port, mode, out_dir):
-    """mode: "ok" | "raise" (rank 1's runner fails) | "vanish" (rank 1 exits
-    without reporting).  Rank 0 writes its outcome to out_dir/rank0.txt."""
+    """mode: "ok" | "raise" (rank 1's runner fails) | "vanish" (the last
+    rank exits without reporting) | "partial" (rank 1 fails on its second
+    pack) | "all_raise" (every runner fails).  Rank 0 writes its outcome to
+    out_dir/rank0.txt: "ok", then per input its index and producing rank,
+    then a line per failed rank; or "failed <rank> <message>"."""
     import numpy as np
 
     from omnivoice_b200.scheduler import WorkerFailed, generate_data_parallel
-    dist = _init(rank, world, port, 10 if mode == "vanish" else 60)
+    dist = _init(rank, world, port, 60)
     inputs = make_inputs()
     seeds = [100 + i for i in range(len(inputs))]
+    calls = []
 
     def runner(batch, decoding, batch_seeds):
-        if mode == "raise" and rank == 1:
+        calls.append(len(batch))
+        if mode == "all_raise" or (mode == "raise" and rank == 1):
             raise RuntimeError("injected failure")
+        if mode == "partial" and rank == 1 and len(calls) == 2:
+            raise RuntimeError("injected failure on the second pack")
         return [(rank, np.full((8, inp.target_frames), s % 1024, np.int32))
                 for inp, s in zip(batch, batch_seeds)]
 
-    if mode == "vanish" and rank == 1:
+    if mode == "vanish" and rank == world - 1:
         os._exit(0)  # leaves between steps, before reporting
     outcome = ""
+    failures = []
     try:
-        res = generate_data_parallel(inputs, FakeDecoding(), seeds, runner, max_rows=1500)
+        res = generate_data_parallel(inputs, FakeDecoding(), seeds, runner, max_rows=1500,
+                                     heartbeat_timeout=3.0, failures=failures)
         if rank == 0:
             lines = []
             for i, (r, codes) in enumerate(res):
                 assert codes.shape == (8, inputs[i].target_frames)
                 assert int(codes[0, 0]) == seeds[i] % 1024
                 lines.append(f"{i} {r}")
+            lines += [f"failure {r} {m}" for r, m in failures]
             outcome = "ok\n" + "\n".join(lines)
+        else:
+            assert res is None
     except WorkerFailed as failure:
         outcome = f"failed {failure.rank} {failure}"
     except Exception:

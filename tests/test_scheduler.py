@@ -69,26 +69,66 @@ def _run(mode, tmp_path, world=2):
     return (tmp_path / "rank0.txt").read_text()
 
 
-def test_two_ranks_gather_results_in_input_order(tmp_path):
-    out = _run("ok", tmp_path)
+def _parse(out):
     assert out.startswith("ok"), out
-    rows = [line.split() for line in out.splitlines()[1:]]
-    assert [int(i) for i, _ in rows] == list(range(10))
-    producers = {int(i): int(r) for i, r in rows}
+    lines = out.splitlines()[1:]
+    producers = {int(a): int(b) for a, b in (l.split() for l in lines if not l.startswith("failure"))}
+    failed = [int(l.split()[1]) for l in lines if l.startswith("failure")]
+    assert sorted(producers) == list(range(10))
+    return producers, failed
+
+
+def _parts(world):
     inputs = dp_workers.make_inputs()
     costs = [utterance_cost(x.length, x.target_frames) for x in inputs]
-    parts, _ = lpt_partition(costs, 2)
+    return lpt_partition(costs, world)[0], costs
+
+
+def test_two_ranks_gather_results_in_input_order(tmp_path):
+    producers, failed = _parse(_run("ok", tmp_path))
+    assert failed == []
+    parts, _ = _parts(2)
     for rank, part in enumerate(parts):
         assert all(producers[i] == rank for i in part)
     assert set(producers.values()) == {0, 1}
 
 
-def test_a_failing_rank_is_reported_by_rank_zero(tmp_path):
-    out = _run("raise", tmp_path)
-    assert out.startswith("failed 1"), out
+def test_a_failing_rank_is_requeued_to_the_survivors(tmp_path):
+    producers, failed = _parse(_run("raise", tmp_path))
+    assert failed == [1]
+    # Every utterance of the failed rank was generated again by rank 0.
+    assert set(producers.values()) == {0}
+
+
+def test_a_rank_that_never_reports_is_requeued(tmp_path):
+    producers, failed = _parse(_run("vanish", tmp_path))
+    assert failed == [1]
+    assert set(producers.values()) == {0}
+
+
+def test_finished_packs_of_a_failing_rank_are_kept(tmp_path):
+    producers, failed = _parse(_run("partial", tmp_path))
+    assert failed == [1]
+    parts, _ = _parts(2)
+    mine = [i for i in parts[1] if producers[i] == 1]
+    assert mine and len(mine) < len(parts[1])  # the first pack's results survive
+    assert all(producers[i] == 0 for i in parts[0])
+
+
+def test_three_ranks_share_the_work_of_one_that_vanished(tmp_path):
+    producers, failed = _parse(_run("vanish", tmp_path, world=3))
+    assert failed == [2]
+    parts, costs = _parts(3)
+    lost = parts[2]
+    # Re-partitioned by LPT over the two survivors.
+    again, _ = lpt_partition([costs[i] for i in lost], 2)
+    for rank, part in enumerate(again):
+        assert all(producers[lost[j]] == rank for j in part)
+    for rank in (0, 1):
+        assert all(producers[i] == rank for i in parts[rank])
+
+
+def test_no_survivor_ends_in_worker_failed(tmp_path):
+    out = _run("all_raise", tmp_path)
+    assert out.startswith("failed "), out
     assert "injected failure" in out
-
-
-def test_a_rank_that_never_reports_ends_in_an_error(tmp_path):
-    out = _run("vanish", tmp_path)
-    assert out.startswith("failed -1"), out
