@@ -108,7 +108,8 @@ def build_test_programs(verbose: bool = False) -> list[Path]:
         if exe.exists() and exe.stat().st_mtime >= max(src.stat().st_mtime, library.stat().st_mtime):
             continue
         cmd = [nvcc(), str(src), "-o", str(exe), "-O2", "-std=c++20", "-I", str(ROOT / "include"),
-               "-I", str(CSRC / "host"), "-L", str(PACKAGE), "-lomnivoice_b200",
+               "-I", str(CSRC / "host"), "-I", str(TESTS / "gufo_shim"),
+               "-L", str(PACKAGE), "-lomnivoice_b200",
                "-Xlinker", "-rpath=$ORIGIN/.."] + ARCH
         result = subprocess.run(cmd, capture_output=True, text=True)
         if verbose or result.returncode != 0:

@@ -12,6 +12,7 @@
 #include "internal.hpp"
 #include "launch.hpp"
 #include "ov_kernels.h"
+#include "norm_device.cuh"
 #include "ptx.cuh"
 #include "synthetic.hpp"
 
@@ -19,39 +20,6 @@ namespace ovb {
 namespace {
 
 constexpr int kRowsPerBlock = 4;  // warps per block, one row each
-
-// Sum of squares -> 1 / sqrt(mean + eps), IEEE sqrt and division so the
-// host oracle can evaluate the same expression.
-__device__ __forceinline__ float rms_scale(float squares, int width, float epsilon) {
-  return 1.0f / sqrtf(squares / static_cast<float>(width) + epsilon);
-}
-
-template <int kVec>  // float4 vectors per lane; width = 128 * kVec
-__device__ __forceinline__ void norm_store_row(const float4 (&x)[kVec], const float* weight,
-                                               __half* out, float scale, int lane) {
-#pragma unroll
-  for (int i = 0; i < kVec; ++i) {
-    const int col = (i * 32 + lane) * 4;
-    const float4 w = *reinterpret_cast<const float4*>(weight + col);
-    uint2 packed;
-    packed.x = pack_half2(w.x * (x[i].x * scale), w.y * (x[i].y * scale));
-    packed.y = pack_half2(w.z * (x[i].z * scale), w.w * (x[i].w * scale));
-    *reinterpret_cast<uint2*>(out + col) = packed;
-  }
-}
-
-template <int kVec>
-__device__ __forceinline__ float row_squares(const float4 (&x)[kVec]) {
-  float s = 0.0f;
-#pragma unroll
-  for (int i = 0; i < kVec; ++i) {
-    s += x[i].x * x[i].x;
-    s += x[i].y * x[i].y;
-    s += x[i].z * x[i].z;
-    s += x[i].w * x[i].w;
-  }
-  return warp_sum(s);
-}
 
 // generator_kernels.hip:62-83 (EmbedKernel) + :85-97 (RmsNormKernel).
 template <int kVec>

@@ -1,0 +1,87 @@
+"""Writes tests/golden/generation_golden.npz: full-shape 32-step CFG
+generations of the CPU oracle (oracle/oracle.cpp, the restatement of the
+reference's Generator::Generate, generator.cpp:486-543) on the default
+28-layer, vocabulary-151936 model with random-init weights of seed 0.
+
+Cases (each with the reference's own noise stream, std::mt19937_64 of its
+seed as in decoding.cpp:64-68,84-85):
+  c1        BASELINE config 1: 40 text ids U[0, 151935] (numpy seed 0),
+            100 masked frames, generation seed 0;
+  c4_<i>    six utterances of the BASELINE config-4 set (64 utterances,
+            numpy seed 4: F ~ U[50, 750], text = round(0.4 F), half with
+            125-250 reference frames), the six with the fewest packed rows
+            (one of them with reference codes); generation seed 1000 + i.
+Per case it stores the conditional ids, audio_start, the frame count, the
+seed and the oracle's codes and unmasked_at ([8][F] int32 each).  The GPU
+test (tests/test_gpu_fullshape.py) generates the same inputs and compares.
+
+Usage: python tests/golden/make_generation_golden.py [--threads N]
+(about 25 minutes on 8 cores).
+"""
+from __future__ import annotations
+
+import argparse
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parents[2]
+sys.path.insert(0, str(ROOT))
+
+VOCAB = 151936
+
+
+def cases():
+    from omnivoice_b200 import ConditionalInput
+    out = []
+    rng = np.random.default_rng(0)
+    inp = ConditionalInput.build(rng.integers(0, VOCAB, size=40).tolist(), None, 100)
+    out.append(("c1", inp, 0))
+    # The config-4 set, drawn exactly as bench.py's batched_set().
+    rng = np.random.default_rng(4)
+    frames = rng.integers(50, 751, size=64)
+    with_ref = set(rng.permutation(64)[:32].tolist())
+    specs = []
+    for i, f in enumerate(frames):
+        ref = int(rng.integers(125, 251)) if i in with_ref else 0
+        specs.append((int(round(0.4 * f)), ref, int(f)))
+    inputs = []
+    for text, ref, target in specs:
+        ids = rng.integers(0, VOCAB, size=text).tolist()
+        codes = rng.integers(0, 1024, size=(8, ref)).astype(np.int32) if ref else None
+        inputs.append(ConditionalInput.build(ids, codes, target))
+    rows = sorted(range(64), key=lambda i: specs[i][0] + specs[i][1] + 2 * specs[i][2])
+    chosen = rows[:6]
+    for i in chosen:
+        out.append((f"c4_{i}", inputs[i], 1000 + i))
+    return out
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--threads", type=int, default=0)
+    args = parser.parse_args()
+    from oracle import binding
+    import os
+    binding.oracle().oc_set_threads(args.threads or os.cpu_count() or 1)
+    model = binding.OracleModel(binding.config(), 0)
+    arrays = {}
+    for name, inp, seed in cases():
+        t0 = time.time()
+        codes, when = model.generate(inp.ids, inp.audio_start, inp.target_frames, seed=seed)
+        arrays[f"{name}_ids"] = inp.ids.astype(np.int32)
+        arrays[f"{name}_meta"] = np.array([inp.audio_start, inp.target_frames, seed], np.int64)
+        arrays[f"{name}_codes"] = codes
+        arrays[f"{name}_unmasked_at"] = when
+        print(f"{name}: L={inp.length} F={inp.target_frames} seed={seed} "
+              f"({time.time() - t0:.0f} s)", flush=True)
+    model.close()
+    path = Path(__file__).with_name("generation_golden.npz")
+    np.savez_compressed(path, names=np.array([n for n, _, _ in cases()]), **arrays)
+    print(f"wrote {path} ({path.stat().st_size} bytes)")
+
+
+if __name__ == "__main__":
+    main()

@@ -91,3 +91,34 @@ def test_cloned_voice_prompts_the_chunks(cuda_device, native, tmp_path):
     gen.close()
     assert [r.codes.shape for r in out] == [(8, 24)] * 3
     assert all(((r.codes >= 0) & (r.codes < 1024)).all() for r in out)
+
+
+def test_gufo_runner_over_the_library(cuda_device, native, tmp_path):
+    """tests/cpp/gufo_runner_test.cpp: a provider/runner translation unit in
+    the shape of the reference's provider.cpp and runner.cpp, built against
+    the Gufo SDK stand-in headers and this library, creates its runner
+    through the registered provider and synthesises a three-chunk request;
+    its codes must match the reference's chunk-by-chunk order."""
+    import subprocess
+
+    from model_files import write_safetensors, write_synthetic_model
+    from omnivoice_b200.build import build_test_programs
+    from oracle import codec as oc
+    exe = [p for p in build_test_programs() if p.name == "gufo_runner_test"][0]
+    cfg = small_config()
+    write_synthetic_model(tmp_path / "model.safetensors", cfg, 3, native)
+    shape = oc.CodecShape(codebook_dim=8, semantic_hidden=32, latent_channels=32,
+                          decoder_channels=256, upsampling_ratios=[2, 3, 4])
+    (tmp_path / "audio_tokenizer").mkdir()
+    write_safetensors(tmp_path / "audio_tokenizer" / "model.safetensors",
+                      oc.synthetic_weights(shape, 2))
+    out = tmp_path / "out"
+    out.mkdir()
+    args = [str(exe), str(tmp_path), str(out), str(cfg.vocab_size), str(cfg.hidden_size),
+            str(cfg.intermediate_size), str(cfg.layers), str(cfg.heads), str(cfg.kv_heads),
+            "8", "32", "32", "256", "2", "3", "4"]
+    run = subprocess.run(args, capture_output=True, text=True, timeout=600)
+    print(run.stdout)
+    assert run.returncode == 0 and run.stdout.strip().endswith("ok"), run.stdout + run.stderr
+    samples = np.fromfile(out / "samples.f32", np.float32)
+    assert samples.shape == (3 * 24 * 24,) and np.isfinite(samples).all()
