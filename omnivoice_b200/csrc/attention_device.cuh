@@ -1,6 +1,4 @@
-// Device building blocks of the tcgen05 flash attention, shared by the
-// standalone attention kernel (attention.cu) and the persistent layer
-// kernel (layers.cu).
+// Device building blocks of the tcgen05 flash attention (attention.cu).
 //
 // One work item = (sequence, one or two 128-query tiles, query head h); kv
 // head = h / (heads / kv_heads).  Three roles:
@@ -28,9 +26,10 @@
 // row sum.
 //
 // Every mbarrier wait takes its phase as (completions of that barrier in
-// earlier work items + uses in this item) & 1, so one set of barriers
-// serves any number of consecutive items (AttnPhase tracks the first
-// term, each role keeping its own copy).
+// earlier work items + uses in this item) & 1, so one set of barriers can
+// serve consecutive items of a CTA (AttnPhase tracks the first term, each
+// role keeping its own copy; a CTA of the kernel in attention.cu runs one
+// item, all counts 0).
 #pragma once
 
 #include <cuda.h>

@@ -5,8 +5,6 @@
 //   embed+norm, 28 x { [norm], QKV GEMM (+QK-norm/RoPE), attention,
 //   o GEMM (+residual), norm, gate/up GEMM (+SwiGLU), down GEMM (+residual) },
 //   gather+final norm, head GEMM, score, select/scatter.
-// Batches of up to kLayerKernelRows packed rows run the 28 layers instead as
-// one persistent kernel (layers.cu) between the embedding and the gather.
 // The whole step is recorded once as a CUDA graph and replayed for every
 // non-empty step; nothing returns to the host between steps (the reference
 // synchronises and selects on the host each step, generator.cpp:517-535).
@@ -33,10 +31,6 @@ namespace ovb {
 namespace {
 
 constexpr float kInitStd = 0.02f;
-// Packed rows up to which the layer stack runs as one persistent kernel
-// (where per-kernel launch costs rival the k loops); OV_LAYER_KERNEL=0 / 1
-// in the environment forces the per-kernel path / the persistent kernel.
-constexpr size_t kLayerKernelRows = 4096;
 
 size_t RoundUp(size_t x, size_t m) { return (x + m - 1) / m * m; }
 
@@ -79,7 +73,6 @@ Engine::Engine(const ov_model_config& config, int device) : cfg_(config), device
   ConfigureGemmKernels();
   ConfigureAttentionKernel();
   ConfigureSelectKernel();
-  ConfigureLayerKernel();
   Check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
   for (auto& e : step_done_)
     Check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
@@ -308,7 +301,6 @@ void Engine::Prepare(const ov_conditional_input* inputs, size_t count,
     }
   }
   cu[n_seqs_] = static_cast<int32_t>(R_);
-  cu_host_ = cu;
   EnsureRope(max_seqlen_);
   // Attention work list: every (sequence, pair of 128-query tiles), longest
   // sequences first so that the long CTAs start in the first wave.
@@ -465,8 +457,7 @@ void Engine::Prepare(const ov_conditional_input* inputs, size_t count,
   // The host vectors above go out of scope: wait for the copies.
   Check(cudaStreamSynchronize(s), "upload batch");
 
-  const std::string signature = sig.str() + "|" + std::to_string(rope_positions_) + "|" +
-                                (LayerKernelWanted() ? "L" : "K");
+  const std::string signature = sig.str() + "|" + std::to_string(rope_positions_);
   if (moved || signature != signature_) {
     DestroyGraph();
     BuildPlans();
@@ -505,100 +496,6 @@ void Engine::BuildPlans() {
            sms_);
   EncodeQkvMap(&qkv_map_, qkv_.get(), QKVW_, R_, QKVW_);
   EncodeAttnOutMap(&attn_out_map_, attn_.get(), QH_, R_, QH_);
-  use_layer_kernel_ = LayerKernelWanted();
-  if (use_layer_kernel_) BuildLayerPlan();
-}
-
-bool Engine::LayerKernelWanted() const {
-  if (!LayerKernelSupports(static_cast<int>(H_), static_cast<int>(cfg_.heads),
-                           static_cast<int>(cfg_.kv_heads), static_cast<int>(D_),
-                           static_cast<int>(I_)) ||
-      cfg_.layers > 255 || R_ == 0)
-    return false;
-  if (const char* env = std::getenv("OV_LAYER_KERNEL")) {
-    if (std::strcmp(env, "0") == 0) return false;
-    if (std::strcmp(env, "1") == 0) return true;
-  }
-  return false;  // measured slower than the per-kernel step (see the design notes)
-}
-
-void Engine::BuildLayerPlan() {
-  const int R = static_cast<int>(R_);
-  const int L = static_cast<int>(cfg_.layers);
-  const int num_m = (R + 127) / 128;
-  const int o_splits = LayerKernelSplits(static_cast<int>(QH_));
-  const int down_splits = LayerKernelSplits(static_cast<int>(I_));
-  std::vector<LayerTask> tasks;
-  std::vector<int32_t> targets;
-  BuildLayerTasks(L, R, static_cast<int>(H_), static_cast<int>(cfg_.heads),
-                  static_cast<int>(cfg_.kv_heads), static_cast<int>(I_), cu_host_, o_splits,
-                  down_splits, &tasks, &targets);
-  const size_t h_tiles = H_ / 256;
-  const size_t counters = static_cast<size_t>(L) * kTaskKinds * num_m;
-  const size_t split_counters = static_cast<size_t>(L) * 2 * num_m * h_tiles;
-  layer_sync_words_ = counters + split_counters + 1;
-  layer_tasks_.Reserve(tasks.size());
-  layer_targets_.Reserve(targets.size());
-  layer_sync_.Reserve(layer_sync_words_);
-  const size_t splits = static_cast<size_t>(std::max(o_splits, down_splits));
-  layer_xchg_.Reserve(std::max<size_t>(num_m * h_tiles * splits * 128 * 256, 4));
-  qkv_odd_.Reserve(R_ * QKVW_);
-  Check(cudaMemcpy(layer_tasks_.get(), tasks.data(), tasks.size() * sizeof(LayerTask),
-                   cudaMemcpyHostToDevice),
-        "upload layer tasks");
-  Check(cudaMemcpy(layer_targets_.get(), targets.data(), targets.size() * sizeof(int32_t),
-                   cudaMemcpyHostToDevice),
-        "upload layer targets");
-  LayerKernelParams& p = layer_params_;
-  p = LayerKernelParams{};
-  const auto half_map = [&](CUtensorMap* m, const uint16_t* base, size_t cols, size_t rows,
-                            uint32_t box_rows) {
-    EncodeTensorMap2D(m, base, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, cols, rows, cols * 2, 64,
-                      box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
-  };
-  half_map(&p.map_normed, normed_.get(), H_, R_, 128);
-  half_map(&p.map_attn, attn_.get(), QH_, R_, 128);
-  half_map(&p.map_act, act_.get(), I_, R_, 128);
-  half_map(&p.map_qkv[0], qkv_.get(), QKVW_, R_, 128);
-  half_map(&p.map_qkv[1], qkv_odd_.get(), QKVW_, R_, 128);
-  EncodeTensorMap2D(&p.map_hidden, hidden_.get(), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, H_, R_, H_ * 4,
-                    32, 128, CU_TENSOR_MAP_SWIZZLE_128B);
-  half_map(&p.map_w_qkv, qkv_w_.get(), H_, L * QKVW_, 256);
-  half_map(&p.map_w_o, o_w_.get(), QH_, L * H_, 256);
-  half_map(&p.map_w_gu, gu_w_.get(), H_, L * 2 * I_, 256);
-  half_map(&p.map_w_down, down_w_.get(), I_, L * H_, 256);
-  p.tasks = layer_tasks_.get();
-  p.ntasks = static_cast<int>(tasks.size());
-  p.num_m = num_m;
-  p.counters = layer_sync_.get();
-  p.targets = layer_targets_.get();
-  p.xchg_counters = layer_sync_.get() + counters;
-  p.xchg = layer_xchg_.get();
-  p.abort = layer_sync_.get() + counters + split_counters;
-  p.err = DeviceErrorWord();
-  p.hidden = hidden_.get();
-  p.normed = normed_.get();
-  p.qkv[0] = qkv_.get();
-  p.qkv[1] = qkv_odd_.get();
-  p.act = act_.get();
-  p.norms = norms_.get();
-  p.positions = positions_.get();
-  p.rope_cos = rope_cos_.get();
-  p.rope_sin = rope_sin_.get();
-  p.max_positions = static_cast<int>(rope_positions_);
-  p.cu_seqlens = cu_seqlens_.get();
-  p.attn_out = attn_.get();
-  p.scale_log2 = 1.0f / std::sqrt(static_cast<float>(D_)) * 1.4426950408889634f;
-  p.epsilon = cfg_.rms_norm_eps;
-  p.rows = R;
-  p.hidden_size = static_cast<int>(H_);
-  p.heads = static_cast<int>(cfg_.heads);
-  p.kv_heads = static_cast<int>(cfg_.kv_heads);
-  p.intermediate = static_cast<int>(I_);
-  p.layers = L;
-  p.o_splits = o_splits;
-  p.down_splits = down_splits;
-  layer_grid_ = LayerKernelGrid();
 }
 
 void Engine::EnqueueForward(cudaStream_t s, Marker* m) {
@@ -624,15 +521,7 @@ void Engine::EnqueueForward(cudaStream_t s, Marker* m) {
               R_, H_, hidden_.get(), LayerNorms(0), eps, normed_.get(), s);
   ++launches;
   const double norm_bytes = R * H * (4 + 2);
-  if (use_layer_kernel_) {
-    const double linear = 2.0 * R * static_cast<double>(H_ * QKVW_ + QH_ * H_ + H_ * 2 * I_ + I_ * H_);
-    mark(kLayerStack, cfg_.layers * (linear + attn_flops), 0.0);
-    Check(cudaMemsetAsync(layer_sync_.get(), 0, layer_sync_words_ * sizeof(uint32_t), s),
-          "clear layer counters");
-    LaunchLayerKernel(layer_params_, layer_grid_, s);
-    ++launches;
-  }
-  for (size_t l = 0; !use_layer_kernel_ && l < cfg_.layers; ++l) {
+  for (size_t l = 0; l < cfg_.layers; ++l) {
     const LayerPlans& p = plans_[l];
     if (l > 0) {
       mark(kRmsNorm, 0.0, norm_bytes);
@@ -710,7 +599,7 @@ const char* KindName(int kind) {
   static const char* names[] = {"embed_norm",      "rmsnorm",      "gemm_qkv_qknorm_rope",
                                 "attention",       "gemm_o_residual", "gemm_gate_up_swiglu",
                                 "gemm_down_residual", "gather_norm", "gemm_audio_head",
-                                "score",           "select", "layer_stack"};
+                                "score",           "select"};
   return names[kind];
 }
 

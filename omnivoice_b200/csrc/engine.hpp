@@ -13,7 +13,6 @@
 
 #include "device_buffer.hpp"
 #include "gemm.hpp"
-#include "layers.hpp"
 #include "ov_generator.h"
 #include "pack.hpp"
 
@@ -51,7 +50,7 @@ class Engine {
   // Kernel classes of a step, in launch order.
   enum Kind {
     kEmbedNorm, kRmsNorm, kGemmQkv, kAttention, kGemmO, kGemmGateUp, kGemmDown,
-    kGatherNorm, kGemmHead, kScore, kSelect, kLayerStack, kKinds
+    kGatherNorm, kGemmHead, kScore, kSelect, kKinds
   };
   // Called before each launch when a step is profiled.
   struct Marker {
@@ -68,8 +67,6 @@ class Engine {
   void AllocateWeights();
   void EnsureRope(size_t positions);
   void BuildPlans();
-  void BuildLayerPlan();
-  bool LayerKernelWanted() const;
   void EnqueueForward(cudaStream_t stream, Marker* marker = nullptr);
   void EnqueueDecode(cudaStream_t stream, Marker* marker = nullptr);
   void EnqueueReset(cudaStream_t stream);
@@ -121,7 +118,6 @@ class Engine {
   // Activations.
   DeviceBuffer<float> hidden_, logits_, conf_;
   DeviceBuffer<uint16_t> normed_, qkv_, attn_, act_, final_;
-  DeviceBuffer<uint16_t> qkv_odd_;  // layer kernel: QKV of odd layers
   DeviceBuffer<int32_t> pred_, codes_, unmasked_;
   DeviceBuffer<uint8_t> gemm_ws_;
   size_t gemm_ws_bytes_ = 0;
@@ -131,17 +127,6 @@ class Engine {
   size_t h2d_bytes_ = 0, d2h_bytes_ = 0;
 
   std::vector<LayerPlans> plans_;
-  // Persistent layer kernel (small batches): task list, dependency
-  // counters (zeroed before each forward), split-K exchange workspace.
-  bool use_layer_kernel_ = false;
-  std::vector<int32_t> cu_host_;
-  DeviceBuffer<LayerTask> layer_tasks_;
-  DeviceBuffer<int32_t> layer_targets_;
-  DeviceBuffer<uint32_t> layer_sync_;  // counters | split counters | abort word
-  size_t layer_sync_words_ = 0;
-  DeviceBuffer<float> layer_xchg_;
-  LayerKernelParams layer_params_{};
-  int layer_grid_ = 0;
   GemmPlan head_plan_;
   CUtensorMap qkv_map_;
   CUtensorMap attn_out_map_;

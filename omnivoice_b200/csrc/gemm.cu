@@ -291,10 +291,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     c.chunk_iter = 0;
     c.joint_iter = 0;
     c.ring = nullptr;
-    c.direct = nullptr;
-    c.direct_ld = 0;
-    c.direct_elem = 0;
-    c.direct_rows = 0;
     c.ep = threadIdx.x - 64;
     c.group = c.ep >> 7;
     c.gep = c.ep & 127;

@@ -1,5 +1,4 @@
-// Device building blocks of the tcgen05 GEMM, shared by the standalone
-// GEMM kernel (gemm.cu) and the persistent layer kernel (layers.cu): tile
+// Device building blocks of the tcgen05 GEMM kernel (gemm.cu): tile
 // constants, the output-tile walk, the fused epilogues (float32 store or
 // residual reduce-add, SwiGLU, QK RMSNorm + RoPE) and the split-K partial
 // exchange through a global workspace.  See gemm.cu for the kernel that
@@ -91,25 +90,7 @@ struct EpilogueCtx {
   // every MMA complete), so each chunk takes its own kStageTile slot of it
   // and no chunk waits for an earlier store to drain.
   uint8_t* ring;         // nullptr: stage through the two staging tiles
-  // Direct mode (non-null): each thread writes its row's pieces straight
-  // from registers to y (128-byte lines; plain stores, or vector reduce-adds
-  // for the residual epilogue) instead of staging a tile for a TMA store.
-  // y's rows are `direct_ld` bytes apart, `direct_elem` bytes per element,
-  // rows at or past `direct_rows` are not written.
-  uint8_t* direct;
-  int64_t direct_ld;
-  int direct_elem;
-  int direct_rows;
 };
-
-// y[row][x ..] += v (32 floats) by 128-bit vector reduce-adds at L2: one
-// writer per element, so the sum is exact and deterministic.
-__device__ __forceinline__ void red_add_v4(float* dst, uint32_t a, uint32_t b, uint32_t c,
-                                           uint32_t d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "r"(a), "r"(b),
-               "r"(c), "r"(d)
-               : "memory");
-}
 
 constexpr uint32_t kGroupBarrier = 1;  // + group: the 128 threads of a group
 constexpr uint32_t kEpiBarrier = 3;    // all 256 epilogue threads
@@ -154,22 +135,6 @@ __device__ __forceinline__ float F4At(const float4& v, int i) {
 template <bool kReduce>
 __device__ __forceinline__ void EmitGroup(EpilogueCtx& c, const CUtensorMap* map,
                                           const uint32_t (&w)[32], int x, int y0, int slot) {
-  if (c.direct != nullptr) {
-    const int row = y0 + c.row;
-    if (row < c.direct_rows) {
-      uint8_t* dst = c.direct + row * c.direct_ld + static_cast<int64_t>(x) * c.direct_elem;
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        if (kReduce)
-          red_add_v4(reinterpret_cast<float*>(dst) + 4 * q, w[4 * q], w[4 * q + 1], w[4 * q + 2],
-                     w[4 * q + 3]);
-        else
-          *reinterpret_cast<uint4*>(dst + 16 * q) =
-              make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
-      }
-    }
-    return;
-  }
   uint8_t* buf;
   const uint32_t bar = kGroupBarrier + static_cast<uint32_t>(c.group);
   if (c.ring != nullptr) {
@@ -200,18 +165,6 @@ __device__ __forceinline__ void EmitGroup(EpilogueCtx& c, const CUtensorMap* map
 // row piece (16 words); thread 0 stores it at column x, row y0.
 __device__ __forceinline__ void EmitJoint(EpilogueCtx& c, const CUtensorMap* map,
                                           const uint32_t (&w)[16], int x, int y0, int slot) {
-  if (c.direct != nullptr) {
-    const int row = y0 + c.row;
-    if (row < c.direct_rows) {
-      uint8_t* dst = c.direct + row * c.direct_ld + static_cast<int64_t>(x) * c.direct_elem +
-                     64 * c.group;
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        *reinterpret_cast<uint4*>(dst + 16 * q) =
-            make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
-    }
-    return;
-  }
   uint8_t* buf;
   if (c.ring != nullptr) {
     buf = c.ring + slot * kStageTile;
@@ -542,15 +495,14 @@ __device__ __forceinline__ void AddOwn(float (&acc)[32], uint32_t taddr) {
   for (int e = 0; e < 32; ++e) acc[e] += __uint_as_float(own[e]);
 }
 
-// kMaxBatch: peers whose slices are loaded together (registers: 32 each).
-template <int BN, int EPI, int S, int kMaxBatch = 2>
+template <int BN, int EPI, int S>
 __device__ __forceinline__ void XchgReduce(const GemmArgs& a, const CUtensorMap* map_y,
                                            EpilogueCtx& c, uint32_t tacc, int tile, int m_tile,
                                            int n_tile, int rank) {
   constexpr int kCols = BN / S;
   constexpr int kSlot4 = kBM * kCols / 4;
   constexpr int kPeers = S - 1;
-  constexpr int kBatch = kPeers < kMaxBatch ? kPeers : kMaxBatch;  // peers' loads in flight together
+  constexpr int kBatch = kPeers < 2 ? kPeers : 2;  // peers' loads in flight together
   const float4* slots =
       reinterpret_cast<const float4*>(a.xchg) + static_cast<size_t>(tile) * S * S * kSlot4;
   const int y0 = m_tile * kBM;

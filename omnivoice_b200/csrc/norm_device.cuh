@@ -1,9 +1,7 @@
-// Row RMSNorm arithmetic shared by the norm kernels (elementwise.cu) and
-// the norm tasks of the persistent layer kernel (layers.cu), so both give
-// bit-identical half rows: one warp per row of 128 * kVec floats, lane l
-// holding float4 vectors l, l + 32, ...; the row's sum of squares is each
-// lane's sum in vector order, then a butterfly over the warp
-// (generator_kernels.hip:85-97).
+// Row RMSNorm arithmetic of the norm kernels (elementwise.cu): one warp per
+// row of 128 * kVec floats, lane l holding float4 vectors l, l + 32, ...;
+// the row's sum of squares is each lane's sum in vector order, then a
+// butterfly over the warp (generator_kernels.hip:85-97).
 #pragma once
 
 #include <cuda_fp16.h>

@@ -43,6 +43,9 @@ _SIG = {
                              _P, _P, _P]),
     "oc_generate": (c_int, [_P, _P, c_size_t, c_size_t, c_size_t, c_size_t, c_float, c_float,
                             c_float, c_float, c_uint64, _P, _P, _P]),
+    "oc_generate_traced": (c_int, [_P, _P, c_size_t, c_size_t, c_size_t, c_size_t, c_float,
+                                   c_float, c_float, c_float, c_uint64, _P, _P, _P, _P, _P, _P]),
+    "oc_set_accumulation_order": (None, [c_int]),
 }
 _REF_SIG = {
     "ref_unmask_schedule": (None, [c_size_t, c_size_t, c_float, _P]),
@@ -146,6 +149,26 @@ class OracleModel:
         if status != 0:
             raise RuntimeError(f"oc_forward failed with {status}")
         return (logits, hidden) if want_hidden else logits
+
+    def generate_traced(self, ids: np.ndarray, audio_start: int, frames: int, steps=32,
+                        seed=0):
+        """generate() with the default decoding settings that also returns,
+        per step, the ids the forward pass saw and the scoring's
+        predictions and confidences."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        c = self.cfg.audio_codebooks
+        codes = np.empty((c, frames), np.int32)
+        when = np.empty((c, frames), np.int32)
+        step_ids = np.zeros((steps, c, ids.shape[1]), np.int32)
+        step_pred = np.zeros((steps, c, frames), np.int32)
+        step_conf = np.zeros((steps, c, frames), np.float32)
+        status = oracle().oc_generate_traced(self.h, ptr(ids), ids.shape[1], audio_start, frames,
+                                             steps, 2.0, 0.1, 5.0, 5.0, seed, None, ptr(codes),
+                                             ptr(when), ptr(step_ids), ptr(step_pred),
+                                             ptr(step_conf))
+        if status != 0:
+            raise RuntimeError(f"oc_generate_traced failed with {status}")
+        return codes, when, step_ids, step_pred, step_conf
 
     def generate(self, ids: np.ndarray, audio_start: int, frames: int, steps=32, guidance=2.0,
                  t_shift=0.1, layer_penalty=5.0, temperature=5.0, seed=0, gumbel=None):

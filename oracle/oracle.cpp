@@ -108,6 +108,8 @@ struct Model {
 
 // ------------------------------------------------------------------- GEMM
 // y[r][o] (+)= sum_k x[r][k] * w[o][k] with float32 accumulation in k order.
+bool g_reversed_sums = false;
+
 void Gemm(const float* x, size_t rows, const Linear& w, float* y, bool accumulate) {
   const size_t in = w.in, out = w.out;
   constexpr size_t kRb = 4, kOb = 256;
@@ -122,7 +124,8 @@ void Gemm(const float* x, size_t rows, const Linear& w, float* y, bool accumulat
       const size_t no = std::min(kOb, out - o0);
       for (size_t i = 0; i < kRb; ++i)
         for (size_t j = 0; j < kOb; ++j) acc[i][j] = 0.0f;
-      for (size_t k = 0; k < in; ++k) {
+      for (size_t kk = 0; kk < in; ++kk) {
+        const size_t k = g_reversed_sums ? in - 1 - kk : kk;
         const float* wr = &w.wt[k * out + o0];
         for (size_t i = 0; i < nr; ++i) {
           const float xv = x[(r0 + i) * in + k];
@@ -500,11 +503,23 @@ size_t oc_select(size_t count, size_t codebooks, size_t frames, const int32_t* p
   return count;
 }
 
+void oc_set_accumulation_order(int reversed) { g_reversed_sums = reversed != 0; }
+
 // generator.cpp:486-543.
 int oc_generate(void* model, const int32_t* ids, size_t length, size_t audio_start,
                 size_t frames, size_t steps, float guidance, float t_shift,
                 float layer_penalty, float temperature, uint64_t seed,
                 const float* gumbel_all, int32_t* codes, int32_t* unmasked_at) {
+  return oc_generate_traced(model, ids, length, audio_start, frames, steps, guidance, t_shift,
+                            layer_penalty, temperature, seed, gumbel_all, codes, unmasked_at,
+                            nullptr, nullptr, nullptr);
+}
+
+int oc_generate_traced(void* model, const int32_t* ids, size_t length, size_t audio_start,
+                       size_t frames, size_t steps, float guidance, float t_shift,
+                       float layer_penalty, float temperature, uint64_t seed,
+                       const float* gumbel_all, int32_t* codes, int32_t* unmasked_at,
+                       int32_t* step_ids, int32_t* step_prediction, float* step_confidence) {
   Model& m = *static_cast<Model*>(model);
   const size_t C = m.cfg.audio_codebooks, V = m.cfg.audio_vocab_size;
   const uint32_t mask = m.cfg.audio_mask_id;
@@ -526,6 +541,12 @@ int oc_generate(void* model, const int32_t* ids, size_t length, size_t audio_sta
     if (status != 0) return status;
     oc_score(logits.data(), C * V, frames, C, V, mask, guidance, prediction.data(),
              confidence.data());
+    if (step_ids != nullptr)
+      std::copy(current.begin(), current.end(), step_ids + step * C * length);
+    if (step_prediction != nullptr)
+      std::copy(prediction.begin(), prediction.end(), step_prediction + step * count);
+    if (step_confidence != nullptr)
+      std::copy(confidence.begin(), confidence.end(), step_confidence + step * count);
     const float* gumbel = nullptr;
     if (temperature > 0.0f) {
       if (gumbel_all != nullptr) {

