@@ -18,16 +18,20 @@ model shape):
 The bars.  Logits within 2e-2 of the fp32-accumulated fp16 restatement
 (north star).  For codes: at random init the 32-step generation is
 chaotic, since near-flat logits make the choice of positions and classes
-flip on float32 rounding, and one early flip changes every later step.
-The fixture measures this on the oracle itself: the same restatement with
-its linear layers' float32 sums in the opposite order (just as valid:
-hipBLAS leaves the order unspecified) is stored with its agreement with
-the oracle.  So the free-running generation is held to agree with the
-oracle at least as well as that second restatement does (or 99.5 %,
-whichever is lower), and the step-by-step comparison (no trajectory
-divergence) to at least the second restatement's prediction agreement
-(or 99 %) and 99 % of the chosen positions.  Every comparison prints its
-figure.
+flip on float32 rounding, and one early flip changes every later step's
+input.  The fixture measures this on the oracle itself: the same
+restatement with its linear layers' float32 sums in the opposite order
+(just as valid: hipBLAS leaves the order unspecified) agrees with the
+oracle on 68 % of config 1's codes, and on 61-100 % of the config-4
+utterances'.  A free-running comparison therefore says where two
+trajectories part, not how close the arithmetic is, so it is reported
+(next to the reversed-sum restatement's figure) and asserted only on
+what does not depend on the trajectory: valid codes and every step
+unmasking exactly its scheduled count.  The parity bar is asserted step
+by step on the oracle's own config-1 trajectory (the same ids into both
+forwards at every step): predictions at the masked positions at least as
+close as the reversed-sum restatement's, or 99 %, and 99 % of the chosen
+positions.  Every comparison prints its figure.
 """
 from __future__ import annotations
 
@@ -42,7 +46,6 @@ from omnivoice_b200 import ConditionalInput, DecodingConfig, Generator, model_co
 pytestmark = pytest.mark.gpu
 
 LOGIT_TOL = 2e-2
-CODE_BAR = 0.995
 VOCAB = 151936
 GOLDEN = Path(__file__).resolve().parent / "golden" / "generation_golden.npz"
 
@@ -73,11 +76,19 @@ def golden(golden_data):
 
 
 def _agreement(name, res, codes, when):
+    """Prints the agreement of a free-running generation with the oracle's
+    and asserts what holds on any trajectory: valid codes, and each step
+    unmasking exactly its scheduled count (decoding.cpp:12-40)."""
+    from oracle import binding
     same_codes = float((res.codes == codes).mean())
     same_when = float((res.unmasked_at == when).mean())
+    parted = [s for s in range(32) if not np.array_equal(res.unmasked_at == s, when == s)]
     print(f"{name}: codes {same_codes:.4f} equal, unmasked_at {same_when:.4f} equal "
-          f"({int((res.codes != codes).sum())} of {codes.size} codes differ)")
+          f"({int((res.codes != codes).sum())} of {codes.size} codes differ; first step "
+          f"choosing other positions: {parted[0] if parted else 'none'})")
     assert ((res.codes >= 0) & (res.codes < 1024)).all()
+    sched = binding.schedule(codes.size, 32, 0.1)
+    assert [int((res.unmasked_at == s).sum()) for s in range(32)] == sched
     return same_codes, same_when
 
 
@@ -87,8 +98,6 @@ def test_generate_config1_full_model_matches_oracle(full, golden, golden_data):
     same_codes, same_when = _agreement("config 1", res, codes, when)
     v_codes, v_when = golden_data["c1_variant_agreement"][:2]
     print(f"config 1: the reversed-sum oracle agrees {v_codes:.4f} / {v_when:.4f}")
-    assert same_codes >= min(v_codes, CODE_BAR)
-    assert same_when >= min(v_when, CODE_BAR)
 
 
 def test_config1_steps_on_the_oracle_trajectory(full, golden, golden_data):
@@ -151,7 +160,6 @@ def test_generate_config4_subset_batch_matches_oracle(full, golden, golden_data)
         v_same += v_codes * codes.size
     print(f"config 4 subset: {same / total:.4f} of {total} codes equal "
           f"(reversed-sum oracle {v_same / total:.4f})")
-    assert same / total >= min(v_same / total, CODE_BAR)
 
 
 def _config_input(text, ref, target, seed):
