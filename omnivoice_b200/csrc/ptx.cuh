@@ -348,13 +348,14 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr, uint32_t lbo_
 }
 
 // Instruction descriptor of tcgen05.mma kind::f16 with f16 A/B, f32 D.
-// b_mn_major selects an MN-major B operand.
+// b_mn_major / a_mn_major select an MN-major B / A operand.
 __host__ __device__ constexpr uint32_t idesc_f16_f32(uint32_t m, uint32_t n,
-                                                     uint32_t b_mn_major = 0) {
+                                                     uint32_t b_mn_major = 0,
+                                                     uint32_t a_mn_major = 0) {
   return (1u << 4)              // D format f32
          | (0u << 7)            // A f16
          | (0u << 10)           // B f16
-         | (0u << 15)           // A K-major
+         | (a_mn_major << 15)   // A major
          | (b_mn_major << 16)   // B major
          | ((n >> 3) << 17)     // N / 8
          | ((m >> 4) << 24);    // M / 16
@@ -502,6 +503,21 @@ __device__ __forceinline__ float warp_max(float v) {
 
 __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Named barrier that also returns the OR of `v` over the `threads` threads
+// meeting at it.
+__device__ __forceinline__ bool named_barrier_or(uint32_t id, uint32_t threads, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\t"
+      "setp.ne.u32 pi, %1, 0;\n\t"
+      "bar.red.or.pred po, %2, %3, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "r"(id), "r"(threads)
+      : "memory");
+  return r != 0;
 }
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {

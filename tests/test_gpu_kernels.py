@@ -324,15 +324,20 @@ def attention_reference(qkv, bounds, heads, kv_heads):
     return out.view(rows, heads * 128)
 
 
-@pytest.mark.parametrize("form", ["pair", "single"])
+@pytest.mark.parametrize("form", ["pair", "pair_t", "single"])
 @pytest.mark.parametrize("lengths,growing", [([1], False), ([5, 127], False), ([128, 129], False),
                                              ([370, 250], False), ([140, 100, 705, 375], False),
-                                             ([1425, 750], False), ([700, 1300], True)])
+                                             ([1425, 750], False), ([700, 1300], True),
+                                             ([257, 384, 1000], True)])
 def test_attention_varlen(monkeypatch, lengths, growing, form):
-    """Both work-item forms, forced through OV_ATTN_FORM: tile pairs (two
-    softmax warpgroups, one query tile each) and single tiles (four softmax
+    """Every work-item form, forced through OV_ATTN_FORM / OV_ATTN_PAIR:
+    tile pairs with O = P V per tile (two softmax warpgroups, one query
+    tile each), tile pairs with the output transposed (pair_t: O^T =
+    V^T P^T, P in shared memory), and single tiles (four softmax
     warpgroups sharing one query tile's keys)."""
-    monkeypatch.setenv("OV_ATTN_FORM", form)
+    monkeypatch.setenv("OV_ATTN_FORM", "single" if form == "single" else "pair")
+    if form == "pair_t":
+        monkeypatch.setenv("OV_ATTN_PAIR", "t")
     g = torch.Generator().manual_seed(sum(lengths))
     heads, kv = 16, 8
     rows = sum(lengths)
