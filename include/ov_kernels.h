@@ -192,6 +192,18 @@ int ov_attention_varlen(const uint16_t* qkv, size_t ld_qkv, size_t rows,
                         size_t heads, size_t kv_heads, size_t head_dim, float scale,
                         uint16_t* out, size_t ld_out, ov_stream_t stream);
 
+/* ov_attention_varlen over an explicit work list, the generator's own form:
+ * items (device, int32 [n_items][2]) = (sequence, first 128-query tile |
+ * tiles per item << 24) with 2 tiles per item (query-tile pairs, run by
+ * one persistent CTA per SM over the units (item, head), items in list
+ * order) or 1 (single tiles, one CTA each; every item must then have 1).
+ * Every query tile of every sequence must be covered exactly once. */
+int ov_attention_varlen_items(const uint16_t* qkv, size_t ld_qkv, size_t rows,
+                              const int32_t* cu_seqlens, size_t num_seqs, size_t max_seqlen,
+                              const int32_t* items, size_t n_items, int single_tiles,
+                              size_t heads, size_t kv_heads, size_t head_dim, float scale,
+                              uint16_t* out, size_t ld_out, ov_stream_t stream);
+
 /* ------------------------------------------------------ decoding tail */
 
 /* generator_kernels.hpp:58-66 (Score).  logits rows [0, frames) are

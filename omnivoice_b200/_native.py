@@ -149,6 +149,8 @@ SIGNATURES: dict[str, tuple] = {
     "ov_gemm_f16_noalloc": (c_int, [_P, _S, _P, _P, _S, _S, _S, _S, c_int, POINTER(EpilogueArgs),
                                     _P]),
     "ov_attention_varlen": (c_int, [_P, _S, _S, _P, _S, _S, _S, _S, _S, c_float, _P, _S, _P]),
+    "ov_attention_varlen_items": (c_int, [_P, _S, _S, _P, _S, _S, _P, _S, c_int, _S, _S, _S,
+                                          c_float, _P, _S, _P]),
     "ov_score": (c_int, [_P, _S, _S, _S, _S, c_uint32, c_float, _P, _P, _P]),
     "ov_select_positions": (c_int, [_P, _P, _S, _S, _S, c_float, c_float, c_int, _P, c_uint64,
                                     c_int32, c_uint32, _P, _P, _P, _S, _S, _S, _P]),

@@ -368,6 +368,54 @@ def test_attention_varlen(monkeypatch, lengths, growing, form):
     assert err.max() < 4e-3 + 4e-3 * ref.abs().max(), float(err.max())
 
 
+def _work_list(lengths, per_item):
+    """The generator's attention work list: (sequence, first tile | tiles
+    per item << 24), longest sequences first."""
+    order = sorted(range(len(lengths)), key=lambda q: -lengths[q])
+    items = []
+    for q in order:
+        for tile in range(0, (lengths[q] + 127) // 128, per_item):
+            items += [q, tile | (per_item << 24)]
+    return torch.tensor(items, dtype=torch.int32)
+
+
+@pytest.mark.parametrize("form", ["pair", "single"])
+@pytest.mark.parametrize("seed,count,lo,hi", [(0, 40, 50, 900), (1, 300, 1, 300),
+                                              (2, 12, 1, 140)])
+def test_attention_work_list(seed, count, lo, hi, form):
+    """The generator's form of the attention: a work list with query-tile
+    pairs run by one persistent CTA per SM (many units per CTA, items of
+    one or two tiles and of one or many key tiles in a row, so every ring
+    stage and barrier phase carries over between items), or single tiles.
+    Against float64."""
+    rng = np.random.default_rng(seed)
+    lengths = [int(v) for v in rng.integers(lo, hi + 1, size=count)]
+    heads, kv = 16, 8
+    rows = sum(lengths)
+    width = (heads + 2 * kv) * 128
+    g = torch.Generator().manual_seed(seed)
+    qkv = (torch.randn(rows, width, generator=g) * 1.5).half()
+    bounds = [0]
+    for n in lengths:
+        bounds.append(bounds[-1] + n)
+    items = _work_list(lengths, 1 if form == "single" else 2)
+    n_items = items.numel() // 2
+    cu = torch.tensor(bounds, dtype=torch.int32).cuda()
+    out = torch.full((rows, heads * 128), float("nan"), device="cuda", dtype=torch.float16)
+    qkv_d, items_d = qkv.cuda(), items.cuda()
+    ok(N.lib().ov_attention_varlen_items(p(qkv_d), width, rows, p(cu), len(lengths),
+                                         max(lengths), p(items_d), n_items,
+                                         1 if form == "single" else 0, heads, kv, 128,
+                                         1.0 / np.sqrt(128), p(out), heads * 128, stream()))
+    torch.cuda.synchronize()
+    assert device_errors() == 0
+    ref = attention_reference(qkv, bounds, heads, kv)
+    got = out.cpu().double()
+    assert torch.isfinite(got).all()
+    err = (got - ref).abs()
+    assert err.max() < 4e-3 + 4e-3 * ref.abs().max(), float(err.max())
+
+
 # ------------------------------------------------------- decoding tail
 
 def test_score_matches_oracle(oracle_lib):
