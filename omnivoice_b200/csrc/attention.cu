@@ -6,10 +6,12 @@
 // writing half probabilities, a batched P V GEMM and MergeHeadsKernel) with
 // one flash-style kernel: scores never leave the SM.  The roles of a work
 // item (softmax warpgroups, producer warp, MMA thread) are in
-// attention_device.cuh; this kernel runs one work item per CTA:
+// attention_device.cuh:
 //   attention_kernel<2>  320 threads: two softmax warpgroups (warps 0-7),
 //                        producer warp 8, MMA warp 9; items of two query
 //                        tiles (one per warpgroup) or one tile split in two;
+//                        with a work list, one persistent CTA per SM runs
+//                        the units (item, head) in turn;
 //   attention_kernel<4>  576 threads: one query tile split over four
 //                        softmax warpgroups (warps 0-15), producer warp 16,
 //                        MMA warp 17.

@@ -28,8 +28,7 @@
 // Every mbarrier wait takes its phase as (completions of that barrier in
 // earlier work items + uses in this item) & 1, so one set of barriers can
 // serve consecutive items of a CTA (AttnPhase tracks the first term, each
-// role keeping its own copy; a CTA of the kernel in attention.cu runs one
-// item, all counts 0).
+// role keeping its own copy and advancing it after every item).
 #pragma once
 
 #include <cuda.h>
