@@ -78,9 +78,16 @@ int ov_graph_capture_end(ov_stream_t stream, ov_graph_t* graph);
 int ov_graph_launch(ov_graph_t graph, ov_stream_t stream);
 int ov_graph_destroy(ov_graph_t graph);
 
-/* Device-side error word written by kernels whose bounded waits ran out
- * (no kernel of this library traps).  Reads and clears it on `device`'s
- * current context; `*flags` is 0 when no wait timed out. */
+/* Bits of the device-side error word. */
+enum {
+  OV_DEVICE_WAIT_TIMEOUT = 1, /* a bounded wait ran out (no kernel of this library traps) */
+  OV_DEVICE_BAD_ARGUMENT = 2  /* an index outside its range was skipped (a RoPE position,
+                                 an attention work item's sequence) */
+};
+
+/* Device-side error word written by kernels (bits above).  Reads and
+ * clears it on the current device's context; `*flags` is 0 when nothing
+ * was reported. */
 int ov_take_device_errors(uint32_t* flags, ov_stream_t stream);
 
 #ifdef __cplusplus

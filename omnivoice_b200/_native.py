@@ -21,6 +21,9 @@ OV_ERR_TIMEOUT = 5
 OV_ERR_CANCELLED = 6
 OV_ERR_IO = 7
 
+OV_DEVICE_WAIT_TIMEOUT = 1
+OV_DEVICE_BAD_ARGUMENT = 2
+
 OV_EPI_STORE_F32 = 0
 OV_EPI_ACCUM_F32 = 1
 OV_EPI_SWIGLU_F16 = 2

@@ -121,6 +121,10 @@ __global__ void __launch_bounds__(ThreadsOf(kWG), 1)
       max_groups = args.single ? 1 : 2;
       h = blockIdx.z;
     }
+    if (seq < 0 || seq >= args.num_seqs) {  // uniform over the CTA; no barrier used
+      if (threadIdx.x == 0) atomicOr(args.err, kErrBadArgument);
+      continue;
+    }
     if (kWG == 4) max_groups = 1;  // the four-warpgroup form takes single tiles only
     const int start = args.cu_seqlens[seq];
     const int len = args.cu_seqlens[seq + 1] - start;
@@ -205,6 +209,10 @@ __global__ void __launch_bounds__(320, 1)
     tile = 2 * blockIdx.x;
   }
   const int h = args.items != nullptr ? static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.z);
+  if (seq < 0 || seq >= args.num_seqs) {  // uniform over the CTA, before any barrier
+    if (threadIdx.x == 0) atomicOr(args.err, kErrBadArgument);
+    return;
+  }
   const int start = args.cu_seqlens[seq];
   const int len = args.cu_seqlens[seq + 1] - start;
   const int q0 = tile * kQ;
@@ -540,6 +548,7 @@ void LaunchAttention(const CUtensorMap& map_qkv, const CUtensorMap& map_out,
   a.cu_seqlens = cu_seqlens;
   a.items = items;
   a.n_items = n_items;
+  a.num_seqs = num_seqs;
   a.out = out;
   a.ld_out = ld_out;
   a.heads = heads;

@@ -103,6 +103,7 @@ struct AttnArgs {
   // `single`), head blockIdx.z.
   const int32_t* items;
   int n_items;
+  int num_seqs;  // entries of cu_seqlens - 1; a work item naming another sequence is skipped
   __half* out;
   int64_t ld_out;
   int heads;

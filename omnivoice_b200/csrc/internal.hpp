@@ -17,8 +17,8 @@
 namespace ovb {
 
 // Bits of the device error word kernels set (see ov_take_device_errors).
-constexpr uint32_t kErrWaitTimeout = 1u;
-constexpr uint32_t kErrBadArgument = 2u;
+constexpr uint32_t kErrWaitTimeout = OV_DEVICE_WAIT_TIMEOUT;
+constexpr uint32_t kErrBadArgument = OV_DEVICE_BAD_ARGUMENT;
 
 // Records `message` as the calling thread's last error and returns status.
 int Fail(int status, const std::string& message);

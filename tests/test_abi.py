@@ -30,6 +30,20 @@ def test_binding_covers_every_declaration():
     assert declared_functions() - {"ov_cancel_fn"} <= set(_native.SIGNATURES)
 
 
+def test_binding_constants_match_the_headers():
+    """Every enumerator the headers define with a plain integer has the same
+    value in the Python binding."""
+    from omnivoice_b200 import _native
+    seen = 0
+    for header in (ROOT / "include").glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", "", header.read_text(), flags=re.S)
+        for m in re.finditer(r"\b(OV_[A-Z0-9_]+)\s*=\s*(\d+)\b", text):
+            if hasattr(_native, m.group(1)):
+                assert getattr(_native, m.group(1)) == int(m.group(2)), m.group(1)
+                seen += 1
+    assert seen >= 10
+
+
 def test_last_error_is_empty_initially(native):
     from omnivoice_b200 import _native
     assert _native.last_error() == "" or isinstance(_native.last_error(), str)

@@ -415,6 +415,29 @@ def test_attention_work_list(seed, count, lo, hi, form):
     assert err.max() < 4e-3 + 4e-3 * ref.abs().max(), float(err.max())
 
 
+def test_attention_work_list_bad_sequence_is_reported():
+    """A work item naming a sequence outside [0, num_seqs) is skipped and
+    reported through the device error word; the valid items still run."""
+    lengths = [200, 90]
+    heads, kv = 16, 8
+    rows = sum(lengths)
+    width = (heads + 2 * kv) * 128
+    g = torch.Generator().manual_seed(5)
+    qkv = (torch.randn(rows, width, generator=g) * 1.5).half()
+    items = torch.cat([_work_list(lengths, 2), torch.tensor([7, 0 | (2 << 24)], dtype=torch.int32)])
+    cu = torch.tensor([0, 200, 290], dtype=torch.int32).cuda()
+    out = torch.zeros((rows, heads * 128), device="cuda", dtype=torch.float16)
+    qkv_d, items_d = qkv.cuda(), items.cuda()
+    assert device_errors() == 0
+    ok(N.lib().ov_attention_varlen_items(p(qkv_d), width, rows, p(cu), 2, 200, p(items_d),
+                                         items.numel() // 2, 0, heads, kv, 128,
+                                         1.0 / np.sqrt(128), p(out), heads * 128, stream()))
+    torch.cuda.synchronize()
+    assert device_errors() == N.OV_DEVICE_BAD_ARGUMENT
+    ref = attention_reference(qkv, [0, 200, 290], heads, kv)
+    assert (out.cpu().double() - ref).abs().max() < 4e-3 + 4e-3 * ref.abs().max()
+
+
 # ------------------------------------------------------- decoding tail
 
 def test_score_matches_oracle(oracle_lib):
