@@ -58,7 +58,8 @@ __device__ __forceinline__ void XchgSplitK(const GemmArgs& a, const CUtensorMap*
     XchgSend<BN, S>(a, tacc, c, tile, rank);
     named_barrier(kEpiBarrier, 256);  // every partial slice is written
     if (c.ep == 0) {
-      __threadfence();
+      // The readers are this cluster's CTAs (acquire at cluster scope).
+      fence_acq_rel_cluster();
       for (int j = 0; j < S; ++j)
         if (j != rank) mbar_arrive_cluster(mapa_shared(smem_u32(inbox_bar), static_cast<uint32_t>(j)));
     }

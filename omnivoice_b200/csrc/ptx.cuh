@@ -407,6 +407,13 @@ __device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst, uint32_t src, ui
       : "memory");
 }
 
+// Orders this thread's earlier memory operations, and those it observed
+// (through a barrier of its CTA), before its later ones, for every thread
+// of the cluster.
+__device__ __forceinline__ void fence_acq_rel_cluster() {
+  asm volatile("fence.acq_rel.cluster;" ::: "memory");
+}
+
 // 16 bytes from registers into another cluster CTA's shared memory
 // (remote_addr from mapa); completes `16` bytes of transaction count on
 // that CTA's mbarrier remote_bar.
