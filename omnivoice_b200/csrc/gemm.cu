@@ -302,23 +302,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     // prologue's cluster barrier, taken while the MMAs run).
     if (kClusterSplit && args.xchg != nullptr) cluster_wait();
     int acc_iter = 0;
-    // This CTA's 128 rows of unit u.
-    auto rows_of = [&](int u) {
-      int m_tile, n_tile, split;
-      UnitCoords(args, u, m_tile, n_tile, split);
-      return PAIR ? 2 * m_tile + static_cast<int>(rank) : m_tile;
-    };
-    // QK-norm epilogue: the RoPE rows of unit u are loaded at the end of
-    // unit u - ustep's epilogue, their positions one unit earlier still.
-    RopeRow rope;
-    if (unit0 < args.units) LoadRopeRow<EPI>(args, RowPosition<EPI>(args, rows_of(unit0), c.row), c.group, rope);
     for (int u = unit0; u < args.units; u += ustep, ++acc_iter) {
       int m_tile, n_tile, split;
       UnitCoords(args, u, m_tile, n_tile, split);
       if constexpr (PAIR) m_tile = 2 * m_tile + static_cast<int>(rank);  // this CTA's 128 rows
       const int buf = acc_iter & 1;
-      const bool more = u + ustep < args.units;
-      const int next_pos = more ? RowPosition<EPI>(args, rows_of(u + ustep), c.row) : 0;
+      RopeRow rope;
+      LoadRopeRow<EPI>(args, m_tile, c.row, c.group, rope);
       // Every epilogue thread runs the epilogue even after a timed-out wait
       // (the error word is set) so the 256 threads stay in step.
       (void)mbar_wait(&tfull[buf], static_cast<uint32_t>(acc_iter >> 1) & 1u, args.err);
@@ -339,7 +329,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       // This CTA's last unit: its loads are all consumed and its MMAs done.
       c.ring = u + ustep >= args.units ? smem : nullptr;
       EpilogueUnit<BN, EPI>(args, &map_y, c, tacc, m_tile, n_tile, norm_w, rope);
-      if (more) LoadRopeRow<EPI>(args, next_pos, c.group, rope);
       tc_fence_before_sync();
       if constexpr (PAIR) {
         // Both CTAs' accumulators are read: one arrival per CTA on rank 0.

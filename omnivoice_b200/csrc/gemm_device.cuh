@@ -97,27 +97,18 @@ constexpr uint32_t kEpiBarrier = 3;    // all 256 epilogue threads
 
 // RoPE cos / sin of one row's position for the 32 rotated pairs this
 // group computes (QK-norm epilogue), loaded before the accumulator is
-// ready so the loads overlap the tile's MMAs.  The row's position is
-// loaded one unit ahead (RowPosition), so the table rows cost one round
-// trip to L2, not two dependent ones.
+// ready so the loads overlap the tile's MMAs.
 struct RopeRow {
   float4 c[8];
   float4 s[8];
 };
 
 template <int EPI>
-__device__ __forceinline__ int RowPosition(const GemmArgs& a, int m_tile, int row) {
+__device__ __forceinline__ void LoadRopeRow(const GemmArgs& a, int m_tile, int row, int group,
+                                            RopeRow& r) {
   if constexpr (EPI == OV_EPI_QKNORM_ROPE_F16) {
     const int64_t grow = static_cast<int64_t>(m_tile) * kBM + row;
-    return grow < a.M ? __ldg(a.positions + grow) : 0;
-  } else {
-    return 0;
-  }
-}
-
-template <int EPI>
-__device__ __forceinline__ void LoadRopeRow(const GemmArgs& a, int pos, int group, RopeRow& r) {
-  if constexpr (EPI == OV_EPI_QKNORM_ROPE_F16) {
+    int pos = grow < a.M ? __ldg(a.positions + grow) : 0;
     if (pos < 0 || pos >= a.max_positions) {
       atomicOr(a.err, kErrBadArgument);
       pos = 0;
