@@ -193,13 +193,13 @@ int ov_attention_varlen(const uint16_t* qkv, size_t ld_qkv, size_t rows,
                         uint16_t* out, size_t ld_out, ov_stream_t stream);
 
 /* ov_attention_varlen over an explicit work list, the generator's own form:
- * items (device, int32 [n_items][2]) = (sequence, first 128-query tile |
- * tiles per item << 24) with 2 tiles per item (query-tile pairs, run by
- * one persistent CTA per SM over the units (item, head), items in list
- * order) or 1 (single tiles, one CTA each; every item must then have 1).
- * Every query tile of every sequence must be covered exactly once; an item
- * naming a sequence outside [0, num_seqs) is skipped and reported as
- * OV_DEVICE_BAD_ARGUMENT by ov_take_device_errors. */
+ * items (device, int32 [n_items][2], at most 65535) = (sequence, first
+ * 128-query tile | tiles per item << 24) with 2 tiles per item (query-tile
+ * pairs) or 1 (single tiles; every item must then have 1), one CTA per
+ * (item, head), items started in list order.  Every query tile of every
+ * sequence must be covered exactly once; an item naming a sequence outside
+ * [0, num_seqs) is skipped and reported as OV_DEVICE_BAD_ARGUMENT by
+ * ov_take_device_errors. */
 int ov_attention_varlen_items(const uint16_t* qkv, size_t ld_qkv, size_t rows,
                               const int32_t* cu_seqlens, size_t num_seqs, size_t max_seqlen,
                               const int32_t* items, size_t n_items, int single_tiles,

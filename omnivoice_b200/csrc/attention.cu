@@ -6,12 +6,10 @@
 // writing half probabilities, a batched P V GEMM and MergeHeadsKernel) with
 // one flash-style kernel: scores never leave the SM.  The roles of a work
 // item (softmax warpgroups, producer warp, MMA thread) are in
-// attention_device.cuh:
+// attention_device.cuh; this kernel runs one work item per CTA:
 //   attention_kernel<2>  320 threads: two softmax warpgroups (warps 0-7),
 //                        producer warp 8, MMA warp 9; items of two query
 //                        tiles (one per warpgroup) or one tile split in two;
-//                        with a work list, one persistent CTA per SM runs
-//                        the units (item, head) in turn;
 //   attention_kernel<4>  576 threads: one query tile split over four
 //                        softmax warpgroups (warps 0-15), producer warp 16,
 //                        MMA warp 17.
@@ -19,7 +17,6 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
-#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstdlib>
@@ -51,6 +48,37 @@ __global__ void __launch_bounds__(ThreadsOf(kWG), 1)
   // inputs (q, k, v of the previous kernel) only after its own set-up.  The
   // work items and sequence bounds are uploaded before the step.
   pdl_trigger();
+  int seq, tile, max_groups;
+  if (args.items != nullptr) {
+    // Work items: head blockIdx.x, item blockIdx.y, so the hardware starts
+    // the items (longest first) in order across all heads.
+    seq = args.items[2 * blockIdx.y];
+    const int code = args.items[2 * blockIdx.y + 1];
+    tile = code & 0xFFFFFF;
+    max_groups = code >> 24;
+  } else if (args.single) {
+    seq = blockIdx.y;
+    tile = blockIdx.x;
+    max_groups = 1;
+  } else {
+    seq = blockIdx.y;
+    tile = 2 * blockIdx.x;
+    max_groups = 2;
+  }
+  if (kWG == 4) max_groups = 1;  // the four-warpgroup form takes single tiles only
+  const int h = args.items != nullptr ? static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.z);
+  if (seq < 0 || seq >= args.num_seqs) {  // uniform over the CTA, before any barrier
+    if (threadIdx.x == 0) atomicOr(args.err, kErrBadArgument);
+    return;
+  }
+  const int start = args.cu_seqlens[seq];
+  const int len = args.cu_seqlens[seq + 1] - start;
+  const int q0 = tile * kQ;
+  if (q0 >= len) return;  // uniform over the CTA, before any barrier
+  const int groups = max_groups >= 2 && q0 + kQ < len ? 2 : 1;
+  const int kvh = h / (args.heads / args.kv_heads);
+  const int nt = (len + kKeys - 1) / kKeys;
+
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -72,17 +100,15 @@ __global__ void __launch_bounds__(ThreadsOf(kWG), 1)
   bars.o_done = bar_mem + 13;   // [2 groups]
   bars.pv_done = bar_mem + 15;  // one query tile: each P V complete
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_mem + 16);
-  bars.q_empty = bar_mem + 17;  // the query buffers free for the next item
   float* xmax = reinterpret_cast<float*>(bar_mem + 18);  // [2 tiles][kWG warpgroups][128 rows]
   float* xsum = xmax + 2 * kWG * 128;                    // [kWG warpgroups][128 rows]
+  const AttnPhase phase;  // fresh barriers: every phase count starts at 0
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  // p_full counts kWG * 128 arrivals per key tile: the threads sharing one
-  // query tile arrive once each, a pair's warpgroup (128 threads) kWG
-  // times each.
   if (threadIdx.x == 0) {
-    InitAttnBars(bars, 128 * kWG);
+    // One query tile: every softmax warpgroup arrives on p_full[i].
+    InitAttnBars(bars, groups == 1 ? 128 * kWG : 128);
     fence_mbar_init();
     tma_prefetch_map(&map_qkv);
     tma_prefetch_map(&map_out);
@@ -97,62 +123,21 @@ __global__ void __launch_bounds__(ThreadsOf(kWG), 1)
   const uint32_t tmem = *tmem_slot;
   pdl_wait();  // q, k, v of the previous kernel are complete
 
-  // Work units: the tile-pair form with a work list is persistent (units
-  // blockIdx.x, + gridDim.x, ...; consecutive units are the heads of one
-  // item, items longest first), so one CTA's next item loads its keys
-  // while the previous one finishes; otherwise one unit per CTA.
-  const bool persistent = kWG == 2 && args.items != nullptr;
-  const int n_units = persistent ? args.n_items * args.heads : 1;
-  AttnPhase phase;  // fresh barriers: every phase count starts at 0
-  bool first = true;
-  for (int u = persistent ? static_cast<int>(blockIdx.x) : 0; u < n_units;
-       u += persistent ? static_cast<int>(gridDim.x) : 1) {
-    int seq, tile, max_groups, h;
-    if (args.items != nullptr) {
-      const int item = persistent ? u / args.heads : static_cast<int>(blockIdx.y);
-      h = persistent ? u % args.heads : static_cast<int>(blockIdx.x);
-      seq = args.items[2 * item];
-      const int code = args.items[2 * item + 1];
-      tile = code & 0xFFFFFF;
-      max_groups = code >> 24;
-    } else {
-      seq = blockIdx.y;
-      tile = args.single ? blockIdx.x : 2 * blockIdx.x;
-      max_groups = args.single ? 1 : 2;
-      h = blockIdx.z;
-    }
-    if (seq < 0 || seq >= args.num_seqs) {  // uniform over the CTA; no barrier used
-      if (threadIdx.x == 0) atomicOr(args.err, kErrBadArgument);
-      continue;
-    }
-    if (kWG == 4) max_groups = 1;  // the four-warpgroup form takes single tiles only
-    const int start = args.cu_seqlens[seq];
-    const int len = args.cu_seqlens[seq + 1] - start;
-    const int q0 = tile * kQ;
-    if (q0 >= len) continue;  // uniform over the CTA; no barrier used
-    const int groups = max_groups >= 2 && q0 + kQ < len ? 2 : 1;
-    const int kvh = h / (args.heads / args.kv_heads);
-    const int nt = (len + kKeys - 1) / kKeys;
-
-    if (warp == kProducerWarp) {
-      AttnProduce(args, &map_qkv, bars, phase, q_s, k_s, v_s, lane, start, q0, groups, nt, h,
-                  kvh, !first);
-    } else if (warp == kMmaWarp) {
-      if (lane == 0)
-        (void)AttnIssue(args, tmem, bars, phase, q_s, k_s, v_s, groups, nt, len - (nt - 1) * kKeys);
-    } else if constexpr (kWG == 4) {
-      SoftmaxRole<4>(args, tmem, bars, phase, xmax, xsum, warp >> 2, warp & 3,
+  if (warp == kProducerWarp) {
+    AttnProduce(args, &map_qkv, bars, phase, q_s, k_s, v_s, lane, start, q0, groups, nt, h, kvh);
+  } else if (warp == kMmaWarp) {
+    if (lane == 0)
+      (void)AttnIssue(args, tmem, bars, phase, q_s, k_s, v_s, groups, nt, len - (nt - 1) * kKeys);
+  } else if constexpr (kWG == 4) {
+    SoftmaxRole<4>(args, &map_out, tmem, bars, phase, xmax, xsum, q_s, warp >> 2, warp & 3, lane,
+                   len, nt, q0, start, h, 1, 1);
+  } else {
+    if (groups == 1)
+      SoftmaxRole<2>(args, &map_out, tmem, bars, phase, xmax, xsum, q_s, warp >> 2, warp & 3,
                      lane, len, nt, q0, start, h, 1, 1);
-    } else {
-      if (groups == 1)
-        SoftmaxRole<2>(args, tmem, bars, phase, xmax, xsum, warp >> 2, warp & 3,
-                       lane, len, nt, q0, start, h, 1, 1);
-      else
-        SoftmaxRole<1>(args, tmem, bars, phase, xmax, xsum, warp >> 2, warp & 3,
-                       lane, len, nt, q0, start, h, 1, 2);
-    }
-    phase.Advance(nt, groups);
-    first = false;
+    else
+      SoftmaxRole<1>(args, &map_out, tmem, bars, phase, xmax, xsum, q_s, warp >> 2, warp & 3,
+                     lane, len, nt, q0, start, h, 1, 1);
   }
   tc_fence_before_sync();
   __syncthreads();
@@ -551,7 +536,6 @@ void LaunchAttention(const CUtensorMap& map_qkv, const CUtensorMap& map_out,
   AttnArgs a;
   a.cu_seqlens = cu_seqlens;
   a.items = items;
-  a.n_items = n_items;
   a.num_seqs = num_seqs;
   a.out = out;
   a.ld_out = ld_out;
@@ -563,24 +547,16 @@ void LaunchAttention(const CUtensorMap& map_qkv, const CUtensorMap& map_out,
   const int per = single ? kQ : 2 * kQ;
   if (items != nullptr && n_items > 65535)
     throw Error(OV_ERR_UNSUPPORTED, "more than 65535 attention work items");
-  // With a work list the tile-pair form runs one persistent CTA per SM
-  // (at most one per unit); the single-tile form one CTA per unit.
-  const int64_t units = static_cast<int64_t>(n_items) * heads;
-  if (items != nullptr && units == 0) return;
-  const bool transposed = !single && PairsWithOutputTransposed();
-  const dim3 grid =
-      items == nullptr
-          ? dim3(static_cast<unsigned>((max_seqlen + per - 1) / per),
-                 static_cast<unsigned>(num_seqs), static_cast<unsigned>(heads))
-      : single || transposed
-          ? dim3(static_cast<unsigned>(heads), static_cast<unsigned>(n_items), 1)
-          : dim3(static_cast<unsigned>(std::min<int64_t>(units, SmCount())), 1, 1);
+  const dim3 grid = items != nullptr
+                        ? dim3(static_cast<unsigned>(heads), static_cast<unsigned>(n_items), 1)
+                        : dim3(static_cast<unsigned>((max_seqlen + per - 1) / per),
+                               static_cast<unsigned>(num_seqs), static_cast<unsigned>(heads));
   if (single) {
     SetMaxDynamicSmem(reinterpret_cast<const void*>(attention_kernel<4>),
                       static_cast<int>(kSmemBytes));
     Launch(attention_kernel<4>, grid, dim3(ThreadsOf(4)), kSmemBytes, stream,
            "attention kernel launch", map_qkv, map_out, a);
-  } else if (transposed) {
+  } else if (PairsWithOutputTransposed()) {
     SetMaxDynamicSmem(reinterpret_cast<const void*>(attention_pair_kernel),
                       static_cast<int>(kPairSmemBytes));
     Launch(attention_pair_kernel, grid, dim3(320), kPairSmemBytes, stream,
@@ -644,7 +620,6 @@ extern "C" int ov_attention_varlen(const uint16_t* qkv, size_t ld_qkv, size_t ro
                     AsStream(stream), single);
   });
 }
-
 extern "C" int ov_attention_varlen_items(const uint16_t* qkv, size_t ld_qkv, size_t rows,
                                          const int32_t* cu_seqlens, size_t num_seqs,
                                          size_t max_seqlen, const int32_t* items, size_t n_items,
@@ -658,8 +633,7 @@ extern "C" int ov_attention_varlen_items(const uint16_t* qkv, size_t ld_qkv, siz
     OV_REQUIRE(ld_out % 8 == 0 && ld_out >= heads * head_dim, "out stride");
     if (rows == 0 || num_seqs == 0 || n_items == 0) return;
     OV_REQUIRE(items != nullptr, "items must not be null");
-    OV_REQUIRE(single_tiles ? n_items <= 65535u : n_items * heads <= static_cast<size_t>(INT32_MAX),
-               "too many work items");
+    OV_REQUIRE(n_items <= 65535u, "too many work items");
     OV_REQUIRE((reinterpret_cast<uintptr_t>(out) & 15u) == 0, "out must be 16-byte aligned");
     CUtensorMap map, map_out;
     EncodeQkvMap(&map, qkv, static_cast<int64_t>(ld_qkv), static_cast<int64_t>(rows),

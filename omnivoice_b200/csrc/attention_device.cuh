@@ -28,7 +28,8 @@
 // Every mbarrier wait takes its phase as (completions of that barrier in
 // earlier work items + uses in this item) & 1, so one set of barriers can
 // serve consecutive items of a CTA (AttnPhase tracks the first term, each
-// role keeping its own copy and advancing it after every item).
+// role keeping its own copy; a CTA of the kernel in attention.cu runs one
+// item, all counts 0).
 #pragma once
 
 #include <cuda.h>
@@ -95,14 +96,10 @@ __device__ __forceinline__ float probs32(const uint32_t (&r)[32], float scale, f
 
 struct AttnArgs {
   const int32_t* cu_seqlens;
-  // [n_items][2] work items (sequence, first 128-query tile | max groups
-  // << 24), longest first; unit u = (item u / heads, head u % heads).  A
-  // CTA of the tile-pair form runs units blockIdx.x, + gridDim.x, ...; the
-  // single-tile form runs unit (blockIdx.y, blockIdx.x).  Or null: sequence
-  // blockIdx.y, tiles 2 blockIdx.x and 2 blockIdx.x + 1 (one tile if
-  // `single`), head blockIdx.z.
+  // [n][2] work items (sequence, first 128-query tile | max groups << 24),
+  // one per blockIdx.y with the head in blockIdx.x; or null: sequence
+  // blockIdx.y, tiles 2 blockIdx.x and 2 blockIdx.x + 1, head blockIdx.z.
   const int32_t* items;
-  int n_items;
   int num_seqs;  // entries of cu_seqlens - 1; a work item naming another sequence is skipped
   __half* out;
   int64_t ld_out;
@@ -124,15 +121,13 @@ struct AttnBars {
   uint64_t* p_full;   // [2] P written over S
   uint64_t* o_done;   // [2] last P V of group g complete
   uint64_t* pv_done;  // [1] one tile: each P V complete
-  uint64_t* q_empty;  // [1] the item's last S MMAs done: the query buffers are free
 };
 
 // Parity of the completions each barrier saw in earlier work items.
 struct AttnPhase {
   enum : int {
     kQFull = 0, kKFull = 1, kKEmpty = 3, kVFull = 5, kVEmpty = 7, kSFull = 9, kPFull = 11,
-    kODone = 13, kPvDone = 15, kQEmpty = 16,
-    kStage1Used = 17  // set: an earlier item used ring stage 1 (two or more key tiles)
+    kODone = 13, kPvDone = 15
   };
   uint32_t bits = 0;
   __device__ __forceinline__ uint32_t operator()(int bar) const { return (bits >> bar) & 1u; }
@@ -141,8 +136,6 @@ struct AttnPhase {
     auto flip = [&](int bar, int count) { bits ^= static_cast<uint32_t>(count & 1) << bar; };
     const int n0 = (nt + 1) / 2, n1 = nt / 2;  // key tiles in ring stage 0 / 1
     flip(kQFull, 1);
-    flip(kQEmpty, 1);
-    if (nt >= 2) bits |= 1u << kStage1Used;
     flip(kKFull, n0);
     flip(kKFull + 1, n1);
     flip(kKEmpty, n0);
@@ -172,7 +165,6 @@ struct AttnPhase {
 // Initial counts of the barriers (one thread, before any use).
 __device__ __forceinline__ void InitAttnBars(const AttnBars& b, int softmax_threads_per_p) {
   mbar_init(b.q_full, 1);
-  mbar_init(b.q_empty, 1);
   for (int i = 0; i < 2; ++i) {
     mbar_init(&b.k_full[i], 1);
     mbar_init(&b.k_empty[i], 1);
@@ -191,14 +183,15 @@ __device__ __forceinline__ void InitAttnBars(const AttnBars& b, int softmax_thre
 // warpgroup; quarter: its warp's tensor-memory lane quarter (warp index
 // % 4).  bar_base: three consecutive named-barrier ids this role may use.
 // Each thread arrives `p_arrive` times on p_full per key tile (p_full's
-// count / the threads that share the tile).  The output goes straight from
-// the registers to global memory, one row per thread.
+// count / the threads that share the tile).  The output goes through the
+// query tiles' shared memory (idle after the last S MMA) by TMA store.
 template <int kParts>
-__device__ __forceinline__ void SoftmaxRole(const AttnArgs& args, uint32_t tmem,
-                                            const AttnBars& bars, const AttnPhase& ph,
-                                            float* xmax, float* xsum, int wg, int quarter,
-                                            int lane, int len, int nt, int q0, int start, int h,
-                                            uint32_t bar_base, uint32_t p_arrive) {
+__device__ __forceinline__ void SoftmaxRole(const AttnArgs& args, const CUtensorMap* map_out_p,
+                                            uint32_t tmem, const AttnBars& bars,
+                                            const AttnPhase& ph, float* xmax, float* xsum,
+                                            uint8_t* q_s, int wg, int quarter, int lane, int len,
+                                            int nt, int q0, int start, int h, uint32_t bar_base,
+                                            uint32_t p_arrive) {
   // With two query tiles warpgroup g owns tile g (S/P and O regions g).
   // With one tile the warpgroups share it ("split"): warpgroup wg takes
   // key columns [kCols wg, kCols (wg + 1)) of every S tile and O columns
@@ -356,26 +349,59 @@ __device__ __forceinline__ void SoftmaxRole(const AttnArgs& args, uint32_t tmem,
     tc_fence_after_sync();
     const float inv = 1.0f / l;
     const int tile_row0 = q0 + g * kQ;
-    // Plain 16-byte stores of this thread's row (rows past the sequence
-    // end belong to the next sequence and are skipped): the query buffers
-    // stay free for the next item's tiles.
-    const bool store = tile_row0 + row < len;
-    __half* dst = args.out + static_cast<int64_t>(start + tile_row0 + row) * args.ld_out + h * kD;
+    if (tile_row0 + kQ <= len) {
+      // Whole tile: O (half) through the tile's Q buffer, idle since its
+      // last S MMA, as 128B-swizzled [128][64] boxes, one TMA store each.
+      uint8_t* stage = q_s + g * kTile;
 #pragma unroll
-    for (int c = 0; c < kChunks; ++c) {
-      const int ocol = col0 + c * 32;
-      uint32_t r[32];
-      tmem_ld_32x32b_x32(o_addr + ocol, r);
-      tmem_ld_wait();
-      if (store) {
+      for (int c = 0; c < kChunks; ++c) {
+        const int ocol = col0 + c * 32;  // output column of this chunk
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(o_addr + ocol, r);
+        tmem_ld_wait();
+        uint8_t* dst = stage + (ocol >> 6) * kHalfTile + row * 128;
 #pragma unroll
-        for (int j = 0; j < 32; j += 8) {
-          float o[8];
+        for (int q = 0; q < 4; ++q) {
+          const int piece = ((ocol & 63) >> 3) + q;  // 16-byte piece within the 128-byte row
+          *reinterpret_cast<uint4*>(dst + ((piece ^ (row & 7)) << 4)) =
+              make_uint4(pack_half2(__uint_as_float(r[8 * q]) * inv, __uint_as_float(r[8 * q + 1]) * inv),
+                         pack_half2(__uint_as_float(r[8 * q + 2]) * inv, __uint_as_float(r[8 * q + 3]) * inv),
+                         pack_half2(__uint_as_float(r[8 * q + 4]) * inv, __uint_as_float(r[8 * q + 5]) * inv),
+                         pack_half2(__uint_as_float(r[8 * q + 6]) * inv, __uint_as_float(r[8 * q + 7]) * inv));
+        }
+      }
+      fence_proxy_async_smem();
+      // Each 64-column half is stored once the warpgroups writing it
+      // (one for a tile pair or a 2-way split, two for a 4-way split) have.
+      constexpr int kWgPerHalf = kParts == 4 ? 2 : 1;
+      named_barrier(split ? bar_base + 1 + (col0 >> 6) : bar_base + 1 + wg, 128 * kWgPerHalf);
+      if (wg % kWgPerHalf == 0 && quarter == 0 && lane == 0) {
+        for (int b = col0 >> 6; b < (col0 >> 6) + halves; ++b)
+          tma_store_2d(map_out_p, stage + b * kHalfTile, h * kD + b * 64, start + tile_row0);
+        bulk_commit_group();
+        bulk_wait_group_read<0>();  // staging read; the writes complete later
+      }
+    } else {
+      // Last, partial tile of a sequence: rows past its end belong to the
+      // next sequence, so plain stores of the valid rows.
+      const bool store = tile_row0 + row < len;
+      __half* dst = args.out + static_cast<int64_t>(start + tile_row0 + row) * args.ld_out + h * kD;
 #pragma unroll
-          for (int e = 0; e < 8; ++e) o[e] = __uint_as_float(r[j + e]) * inv;
-          *reinterpret_cast<uint4*>(dst + ocol + j) =
-              make_uint4(pack_half2(o[0], o[1]), pack_half2(o[2], o[3]),
-                         pack_half2(o[4], o[5]), pack_half2(o[6], o[7]));
+      for (int c = 0; c < kChunks; ++c) {
+        const int ocol = col0 + c * 32;
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(o_addr + ocol, r);
+        tmem_ld_wait();
+        if (store) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            float o[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) o[e] = __uint_as_float(r[j + e]) * inv;
+            *reinterpret_cast<uint4*>(dst + ocol + j) =
+                make_uint4(pack_half2(o[0], o[1]), pack_half2(o[2], o[3]),
+                           pack_half2(o[4], o[5]), pack_half2(o[6], o[7]));
+          }
         }
       }
     }
@@ -384,15 +410,13 @@ __device__ __forceinline__ void SoftmaxRole(const AttnArgs& args, uint32_t tmem,
 
 // The producer warp's part of a work item: lane 0 loads the query tiles
 // and the K tiles, lane 1 the V tiles, each into a 2-deep ring; stage
-// t & 1 is refilled once the MMAs reading it are done.  wait_q: an earlier
-// item of this CTA ran, so the query buffers are loaded once its last S
-// MMAs completed and the first two stages once its MMAs consumed them.
-// Each lane lets its copies land before returning.
+// t & 1 is refilled once the MMAs reading it are done.  Each lane lets its
+// copies land before returning.
 __device__ __forceinline__ void AttnProduce(const AttnArgs& args, const CUtensorMap* map_qkv,
                                             const AttnBars& bars, const AttnPhase& ph,
                                             uint8_t* q_s, uint8_t* k_s, uint8_t* v_s, int lane,
                                             int start, int q0, int groups, int nt, int h,
-                                            int kvh, bool wait_q) {
+                                            int kvh) {
   if (lane >= 2) return;
   const bool keys = lane == 0;
   const int col = keys ? (args.heads + kvh) * kD : (args.heads + args.kv_heads + kvh) * kD;
@@ -403,8 +427,6 @@ __device__ __forceinline__ void AttnProduce(const AttnArgs& args, const CUtensor
   uint8_t* ring = keys ? k_s : v_s;
   if (keys) {
     const int qcol = h * kD;
-    // Completion number (items so far - 1) of q_empty: parity ph ^ 1.
-    if (wait_q && !mbar_wait(bars.q_empty, ph(AttnPhase::kQEmpty) ^ 1u, args.err)) return;
     mbar_arrive_expect_tx(bars.q_full, groups * kTile);
     for (int g = 0; g < groups; ++g) {
       tma_load_2d(q_s + g * kTile, map_qkv, bars.q_full, qcol, start + q0 + g * kQ);
@@ -415,10 +437,7 @@ __device__ __forceinline__ void AttnProduce(const AttnArgs& args, const CUtensor
   int issued = 0;
   for (int t = 0; t < nt; ++t) {
     const int st = t & 1;
-    // A stage is free once its previous use (in this item, or for the
-    // first two tiles in an earlier item, if any used it) was consumed.
-    const bool reused = t >= 2 || (wait_q && (st == 0 || ph(AttnPhase::kStage1Used)));
-    if (reused && !mbar_wait(&empty[st],
+    if (t >= 2 && !mbar_wait(&empty[st],
                              ph(empty_bit + st) ^ (static_cast<uint32_t>((t >> 1) - 1) & 1u),
                              args.err))
       break;
@@ -472,7 +491,6 @@ __device__ __forceinline__ bool AttnIssue(const AttnArgs& args, uint32_t tmem, c
       }
       umma_commit(&bars.s_full[t & 1]);
       umma_commit(&bars.k_empty[t & 1]);  // K(t) consumed
-      if (t == nt - 1) umma_commit(bars.q_empty);  // Q read by its last MMAs
     };
     auto issue_pv1 = [&](int t) {
       const uint32_t va = smem_u32(v_s + (t & 1) * kTile);
@@ -550,7 +568,6 @@ __device__ __forceinline__ bool AttnIssue(const AttnArgs& args, uint32_t tmem, c
   tc_fence_after_sync();
   for (int g = 0; g < groups; ++g) issue_s(g, 0);
   umma_commit(&bars.k_empty[0]);
-  if (nt == 1) umma_commit(bars.q_empty);  // Q read by its last MMAs
   for (int t = 0; t < nt; ++t) {
     const bool more = t + 1 < nt;
     for (int g = 0; g < groups; ++g) {
@@ -570,7 +587,6 @@ __device__ __forceinline__ bool AttnIssue(const AttnArgs& args, uint32_t tmem, c
     }
     umma_commit(&bars.v_empty[t & 1]);
     if (more) umma_commit(&bars.k_empty[(t + 1) & 1]);
-    if (t + 2 == nt) umma_commit(bars.q_empty);  // Q read by its last MMAs
   }
   return true;
 }

@@ -382,10 +382,9 @@ def _work_list(lengths, per_item):
 @pytest.mark.parametrize("seed,count,lo,hi", [(0, 40, 50, 900), (1, 300, 1, 300),
                                               (2, 12, 1, 140)])
 def test_attention_work_list(seed, count, lo, hi, form):
-    """The generator's form of the attention: a work list with query-tile
-    pairs run by one persistent CTA per SM (many units per CTA, items of
-    one or two tiles and of one or many key tiles in a row, so every ring
-    stage and barrier phase carries over between items), or single tiles.
+    """The generator's form of the attention: a work list of query-tile
+    pairs (items of one or two tiles, one or many key tiles, the last key
+    tile cut at any length) or of single tiles, one CTA per (item, head).
     Against float64."""
     rng = np.random.default_rng(seed)
     lengths = [int(v) for v in rng.integers(lo, hi + 1, size=count)]
