@@ -126,8 +126,7 @@ __global__ void __launch_bounds__(ThreadsOf(kWG), 1)
   if (warp == kProducerWarp) {
     AttnProduce(args, &map_qkv, bars, phase, q_s, k_s, v_s, lane, start, q0, groups, nt, h, kvh);
   } else if (warp == kMmaWarp) {
-    if (lane == 0)
-      (void)AttnIssue(args, tmem, bars, phase, q_s, k_s, v_s, groups, nt, len - (nt - 1) * kKeys);
+    if (lane == 0) (void)AttnIssue(args, tmem, bars, phase, q_s, k_s, v_s, groups, nt);
   } else if constexpr (kWG == 4) {
     SoftmaxRole<4>(args, &map_out, tmem, bars, phase, xmax, xsum, q_s, warp >> 2, warp & 3, lane,
                    len, nt, q0, start, h, 1, 1);
@@ -335,14 +334,11 @@ __global__ void __launch_bounds__(320, 1)
         if (!ok) break;
         tc_fence_after_sync();
         const uint32_t va = smem_u32(ring + (vp % kRing) * kTile);
-        // The last key tile stops at its last 16-key step inside the sequence.
-        const int kks = t == nt - 1 ? (len - t * kKeys + 15) / 16 : kKeys / 16;
 #pragma unroll
         for (int kk = 0; kk < kKeys / 16; ++kk)
-          if (kk < kks)
-            umma_f16_ss(tmem + 256, smem_desc_sw128(va + kk * 16 * 128, kHalfTile, 1024),
-                        smem_desc_sw128(pa + (kk >> 2) * kPBox + (kk & 3) * 32, 16, 1024),
-                        idesc_o, (t > 0 || kk > 0) ? 1u : 0u);
+          umma_f16_ss(tmem + 256, smem_desc_sw128(va + kk * 16 * 128, kHalfTile, 1024),
+                      smem_desc_sw128(pa + (kk >> 2) * kPBox + (kk & 3) * 32, 16, 1024), idesc_o,
+                      (t > 0 || kk > 0) ? 1u : 0u);
         umma_commit(pv_done);
         umma_commit(&empty[vp % kRing]);
         if (t == nt - 1) umma_commit(o_done);

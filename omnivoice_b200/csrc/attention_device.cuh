@@ -456,12 +456,10 @@ __device__ __forceinline__ void AttnProduce(const AttnArgs& args, const CUtensor
 }
 
 // The MMA thread's part of a work item (see the file comment for the two
-// schedules).  last_keys: the keys of the last key tile inside the
-// sequence; its P V stops at the last 16-key step holding one (the
-// probabilities past it are 0).  Returns false when a bounded wait gave up.
+// schedules).  Returns false when a bounded wait gave up.
 __device__ __forceinline__ bool AttnIssue(const AttnArgs& args, uint32_t tmem, const AttnBars& bars,
                                           const AttnPhase& ph, uint8_t* q_s, uint8_t* k_s,
-                                          uint8_t* v_s, int groups, int nt, int last_keys) {
+                                          uint8_t* v_s, int groups, int nt) {
   constexpr uint32_t idesc_s = idesc_f16_f32(kQ, kKeys, 0);
   constexpr uint32_t idesc_o = idesc_f16_f32(kQ, kD, 1);
   const uint32_t qa = smem_u32(q_s);
@@ -496,13 +494,11 @@ __device__ __forceinline__ bool AttnIssue(const AttnArgs& args, uint32_t tmem, c
       const uint32_t va = smem_u32(v_s + (t & 1) * kTile);
       const uint32_t p = tmem + static_cast<uint32_t>((t & 1) * 256);
       const uint32_t o = tmem + 128;
-      const int kks = t == nt - 1 ? (last_keys + 15) / 16 : kKeys / 16;
 #pragma unroll
       for (int kk = 0; kk < kKeys / 16; ++kk)
-        if (kk < kks)
-          umma_f16_ts(o, p + static_cast<uint32_t>(kk * 8),
-                      smem_desc_sw128(va + kk * 16 * 128, kHalfTile, 1024), idesc_o,
-                      (t > 0 || kk > 0) ? 1u : 0u);
+        umma_f16_ts(o, p + static_cast<uint32_t>(kk * 8),
+                    smem_desc_sw128(va + kk * 16 * 128, kHalfTile, 1024), idesc_o,
+                    (t > 0 || kk > 0) ? 1u : 0u);
       umma_commit(bars.pv_done);
       if (t == nt - 1) umma_commit(&bars.o_done[0]);
       umma_commit(&bars.v_empty[t & 1]);  // V(t) consumed
@@ -557,13 +553,11 @@ __device__ __forceinline__ bool AttnIssue(const AttnArgs& args, uint32_t tmem, c
     const uint32_t va = smem_u32(v_s + (t & 1) * kTile);
     const uint32_t p = tmem + static_cast<uint32_t>(g * 256);
     const uint32_t o = p + 128;
-    const int kks = t == nt - 1 ? (last_keys + 15) / 16 : kKeys / 16;
 #pragma unroll
     for (int kk = 0; kk < kKeys / 16; ++kk)
-      if (kk < kks)
-        umma_f16_ts(o, p + static_cast<uint32_t>(kk * 8),
-                    smem_desc_sw128(va + kk * 16 * 128, kHalfTile, 1024), idesc_o,
-                    (t > 0 || kk > 0) ? 1u : 0u);
+      umma_f16_ts(o, p + static_cast<uint32_t>(kk * 8),
+                  smem_desc_sw128(va + kk * 16 * 128, kHalfTile, 1024), idesc_o,
+                  (t > 0 || kk > 0) ? 1u : 0u);
   };
   tc_fence_after_sync();
   for (int g = 0; g < groups; ++g) issue_s(g, 0);
