@@ -72,6 +72,8 @@ struct GemmShapeChoice {
 // OV_GEMM_TILE=<bn>x<splits> (serialised split-K), <bn>c<splits> (cluster
 // split-K) or <bn>p1 (CTA pairs) in the environment overrides the choice
 // (tuning aid; ignored when the override is not valid for the product).
+// OV_GEMM_XCHG=0 makes cluster split-K exchange its partials through
+// distributed shared memory even when a workspace is given.
 // allow_xchg false: with a workspace, only its order-counter use (serialised
 // split-K) is considered, never the partial-slice exchange.
 GemmShapeChoice ChooseGemmShape(int M, int N, int K, int epilogue, bool have_workspace, int sms,
