@@ -386,7 +386,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           (void)mbar_wait(inbox_bar, 0, args.err);
           __syncwarp();
           ClusterReduce<BN, EPI>(args, &map_y, c, tacc, smem, m_tile, n_tile, split);
-          // No CTA leaves while a peer may still be writing into the cluster.
+          // No CTA leaves while a peer's bulk copy may still read its outbox.
           __syncwarp();
           cluster_sync();
         }
@@ -449,9 +449,9 @@ bool ValidShape(int bn, int splits, bool cluster, int N, int K, int epilogue, bo
     if (splits != 2 && splits != 4 && splits != 8) return false;
     if (epilogue != OV_EPI_ACCUM_F32 && epilogue != OV_EPI_STORE_F32) return false;
     if (bn / splits < 32 || (K / kBK) < splits) return false;
-    // Distributed shared memory: the inbox, S - 1 slices, lives in the
-    // 192 KB operand ring.
-    if (!xchg && (splits - 1) * kBM * (bn / splits) * 4 > kRingBytes) return false;
+    // Distributed shared memory: inbox and outbox, (S - 1) slices each,
+    // live in the 192 KB operand ring.
+    if (!xchg && 2 * (splits - 1) * kBM * (bn / splits) * 4 > kRingBytes) return false;
     return bn == 64 || bn == 128 || bn == 256;
   }
   if (splits > 1 && (epilogue != OV_EPI_ACCUM_F32 || (K / kBK) / splits < 2)) return false;

@@ -346,41 +346,50 @@ __device__ __forceinline__ void EpilogueUnit(const GemmArgs& a, const CUtensorMa
 
 // Cluster split-K.  After every CTA of the cluster has finished its MMAs
 // (a cluster barrier), the idle operand ring of each CTA holds an inbox of
-// S - 1 slots, each [128 rows][BN / S] floats with 16-byte pieces
-// XOR-swizzled by row.  Rank r owns column slice r of the tile.
+// S - 1 slots followed by an outbox of S - 1 slots, each [128 rows][BN / S]
+// floats with 16-byte pieces XOR-swizzled by row.  Rank r owns column slice
+// r of the tile.
 
 // Slot of rank `other` among the S - 1 ranks other than `self`.
 __device__ __forceinline__ int PeerSlot(int other, int self) { return other < self ? other : other - 1; }
 
 // Step 1: every other rank's slice of this CTA's partial goes from tensor
-// memory straight into that rank's inbox (its idle operand ring: slot
-// PeerSlot(this rank, that rank)), 16 bytes per st.async, each completing
-// on that rank's inbox barrier; the two epilogue groups take alternate
-// 32-column chunks.  Slot layout: [row][BN / S floats], 16-byte pieces
-// XOR-swizzled by row.
+// memory into the outbox (the two epilogue groups take alternate 32-column
+// chunks); then one thread sends each outbox slot to its rank's inbox with
+// a bulk copy that completes on that rank's inbox barrier.
 template <int BN>
 __device__ __forceinline__ void ClusterSend(uint32_t tacc, uint8_t* ring, const EpilogueCtx& c,
                                             int rank, int splits, uint64_t* inbox_bar) {
   const int cols = BN / splits;
   const uint32_t slot_bytes = static_cast<uint32_t>(kBM * cols * 4);
-  const uint32_t inbox = smem_u32(ring);
+  uint8_t* outbox = ring + (splits - 1) * slot_bytes;
   int chunk = 0;
 #pragma unroll 1
   for (int j = 0; j < splits; ++j) {
     if (j == rank) continue;
-    const uint32_t slot = mapa_shared(inbox + PeerSlot(rank, j) * slot_bytes, static_cast<uint32_t>(j));
-    const uint32_t bar = mapa_shared(smem_u32(inbox_bar), static_cast<uint32_t>(j));
+    uint8_t* slot = outbox + PeerSlot(j, rank) * slot_bytes;
 #pragma unroll 1
     for (int cc = 0; cc < cols; cc += 32, ++chunk) {
       if ((chunk & 1) != c.group) continue;  // uniform over the group
       uint32_t v[32];
       tmem_ld_32x32b_x32(tacc + static_cast<uint32_t>(j * cols + cc), v);
       tmem_ld_wait();
-      const uint32_t dst = slot + static_cast<uint32_t>((c.row * cols + cc) * 4);
+      uint8_t* dst = slot + (c.row * cols + cc) * 4;
 #pragma unroll
       for (int q = 0; q < 8; ++q)
-        st_async_v4(dst + static_cast<uint32_t>((q ^ (c.row & 7)) << 4),
-                    make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]), bar);
+        *reinterpret_cast<uint4*>(dst + ((q ^ (c.row & 7)) << 4)) =
+            make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    }
+  }
+  fence_proxy_async_smem();
+  named_barrier(kEpiBarrier, 256);
+  if (c.ep == 0) {
+    const uint32_t inbox = smem_u32(ring);
+    for (int j = 0; j < splits; ++j) {
+      if (j == rank) continue;
+      const uint32_t src = smem_u32(outbox + PeerSlot(j, rank) * slot_bytes);
+      const uint32_t dst = mapa_shared(inbox + PeerSlot(rank, j) * slot_bytes, j);
+      bulk_copy_to_peer(dst, src, slot_bytes, mapa_shared(smem_u32(inbox_bar), j));
     }
   }
 }

@@ -414,17 +414,6 @@ __device__ __forceinline__ void fence_acq_rel_cluster() {
   asm volatile("fence.acq_rel.cluster;" ::: "memory");
 }
 
-// 16 bytes from registers into another cluster CTA's shared memory
-// (remote_addr from mapa); completes `16` bytes of transaction count on
-// that CTA's mbarrier remote_bar.
-__device__ __forceinline__ void st_async_v4(uint32_t remote_addr, const uint4& v,
-                                            uint32_t remote_bar) {
-  asm volatile(
-      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];"
-      ::"r"(remote_addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(remote_bar)
-      : "memory");
-}
-
 // --------------------------------------------------- CTA pairs (cta_group::2)
 //
 // A CTA pair (a cluster of two) runs one tcgen05.mma of M = 256: each CTA

@@ -256,7 +256,8 @@ def test_gemm_every_tile_shape(monkeypatch, tile, epi):
     assert torch.equal(outs[0], outs[1])
     if "c" in tile:
         assert torch.equal(outs[2], outs[3])
-        assert torch.equal(outs[0], outs[2])
+        if tile != "256c8":  # its slices do not fit the operand ring twice: no shared-memory form
+            assert torch.equal(outs[0], outs[2])
 
 
 @pytest.mark.parametrize("tile", [None, "256x1", "256p1"])
