@@ -260,6 +260,42 @@ def test_gemm_every_tile_shape(monkeypatch, tile, epi):
             assert torch.equal(outs[0], outs[2])
 
 
+def test_gemm_order_counter_wait_times_out_and_reports(monkeypatch):
+    """Failure detection without a GPU fault.  Serialised split-K adds each
+    split into y behind a per-tile order counter in the caller's workspace,
+    which the caller must zero before first use; every wait on it is
+    bounded (2 s).  A workspace left dirty never shows the expected count:
+    the waits run out, the kernel still ends and reports
+    OV_DEVICE_WAIT_TIMEOUT through the device error word, and the next call
+    on a zeroed workspace is exact again."""
+    import time
+    monkeypatch.setenv("OV_GEMM_TILE", "128x4")
+    g = torch.Generator().manual_seed(3)
+    M, N_, K = 200, 512, 1024
+    x = torch.randn(M, K, generator=g).half().cuda()
+    w = (torch.randn(N_, K, generator=g) * 0.02).half().cuda()
+    base = torch.randn(M, N_, generator=g).cuda()
+    need = N.lib().ov_gemm_workspace_bytes(M, K, N_, N.OV_EPI_ACCUM_F32)
+    assert need > 0
+    ws = torch.full((need,), 0x55, dtype=torch.uint8, device="cuda")
+    assert device_errors() == 0
+    y = base.clone()
+    start = time.monotonic()
+    gemm(x, w, y, N.OV_EPI_ACCUM_F32, workspace=ws)
+    torch.cuda.synchronize()
+    elapsed = time.monotonic() - start
+    assert device_errors() & N.OV_DEVICE_WAIT_TIMEOUT
+    assert 1.0 < elapsed < 60.0, elapsed
+    ws.zero_()
+    y = base.clone()
+    gemm(x, w, y, N.OV_EPI_ACCUM_F32, workspace=ws)
+    torch.cuda.synchronize()
+    assert device_errors() == 0
+    ref = x.double().cpu() @ w.double().cpu().T + base.double().cpu()
+    bound = K * 2.0 ** -23 * (x.double().abs().cpu() @ w.double().abs().cpu().T) + 1e-5 * base.double().abs().cpu() + 1e-6
+    assert ((y.cpu().double() - ref).abs() <= bound).all()
+
+
 @pytest.mark.parametrize("tile", [None, "256x1", "256p1"])
 def test_gemm_swiglu_epilogue(monkeypatch, tile):
     if tile:
