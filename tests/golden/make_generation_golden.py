@@ -7,6 +7,8 @@ Cases (each with the reference's own noise stream, std::mt19937_64 of its
 seed as in decoding.cpp:64-68,84-85):
   c1        BASELINE config 1: 40 text ids U[0, 151935] (numpy seed 0),
             100 masked frames, generation seed 0;
+  c2        BASELINE config 2: 120 text ids U[0, 151935] (numpy seed 1),
+            250 masked frames, generation seed 1;
   c4_<i>    six utterances of the BASELINE config-4 set (64 utterances,
             numpy seed 4: F ~ U[50, 750], text = round(0.4 F), half with
             125-250 reference frames), the six with the fewest packed rows
@@ -15,9 +17,9 @@ Per case it stores the conditional ids, audio_start, the frame count, the
 seed and the oracle's codes and unmasked_at ([8][F] int32 each).  The GPU
 test (tests/test_gpu_fullshape.py) generates the same inputs and compares.
 
-For config 1 it also stores the oracle's trajectory: per step the ids the
-forward pass saw and the scoring's predictions and confidences, so the GPU
-can be compared step by step on identical inputs.
+For configs 1 and 2 it also stores the oracle's trajectory: per step the
+ids the forward pass saw and the scoring's predictions and confidences, so
+the GPU can be compared step by step on identical inputs.
 
 The bar the comparisons are held to comes from the oracle itself, run
 with its linear layers' float32 sums in the opposite order
@@ -27,8 +29,9 @@ Stored per case: that variant's agreement with the oracle (codes and
 unmasked_at of the free-running generation) and, for config 1, its
 per-step prediction agreement on the oracle's trajectory.
 
-Usage: python tests/golden/make_generation_golden.py [--threads N]
-(about 50 minutes on 8 cores).
+Usage: python tests/golden/make_generation_golden.py [--threads N] [--only NAME ...]
+(about 50 minutes on 8 cores for every case; --only recomputes the named
+cases and keeps the others already in the file).
 """
 from __future__ import annotations
 
@@ -51,6 +54,9 @@ def cases():
     rng = np.random.default_rng(0)
     inp = ConditionalInput.build(rng.integers(0, VOCAB, size=40).tolist(), None, 100)
     out.append(("c1", inp, 0))
+    rng = np.random.default_rng(1)
+    inp = ConditionalInput.build(rng.integers(0, VOCAB, size=120).tolist(), None, 250)
+    out.append(("c2", inp, 1))
     # The config-4 set, drawn exactly as bench.py's batched_set().
     rng = np.random.default_rng(4)
     frames = rng.integers(50, 751, size=64)
@@ -74,14 +80,20 @@ def cases():
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--threads", type=int, default=0)
+    parser.add_argument("--only", nargs="*", default=None)
     args = parser.parse_args()
     from oracle import binding
     import os
     binding.oracle().oc_set_threads(args.threads or os.cpu_count() or 1)
     model = binding.OracleModel(binding.config(), 0)
     lib = binding.oracle()
+    path = Path(__file__).with_name("generation_golden.npz")
     arrays = {}
+    if args.only is not None and path.exists():
+        arrays = {k: v for k, v in np.load(path).items() if k != "names"}
     for name, inp, seed in cases():
+        if args.only is not None and name not in args.only:
+            continue
         t0 = time.time()
         lib.oc_set_accumulation_order(0)
         codes, when, step_ids, step_pred, step_conf = model.generate_traced(
@@ -94,10 +106,10 @@ def main() -> None:
         lib.oc_set_accumulation_order(1)
         v_codes, v_when = model.generate(inp.ids, inp.audio_start, inp.target_frames, seed=seed)
         agreement = [float((v_codes == codes).mean()), float((v_when == when).mean())]
-        if name == "c1":
-            arrays["c1_step_ids"] = step_ids
-            arrays["c1_step_prediction"] = step_pred
-            arrays["c1_step_confidence"] = step_conf
+        if name in ("c1", "c2"):
+            arrays[f"{name}_step_ids"] = step_ids
+            arrays[f"{name}_step_prediction"] = step_pred
+            arrays[f"{name}_step_confidence"] = step_conf
             # ... and step by step on the oracle's own trajectory.
             same = total = 0
             for step in range(step_ids.shape[0]):
@@ -114,7 +126,6 @@ def main() -> None:
         print(f"{name}: L={inp.length} F={inp.target_frames} seed={seed}, reversed-sum "
               f"restatement agrees {agreement} ({time.time() - t0:.0f} s)", flush=True)
     model.close()
-    path = Path(__file__).with_name("generation_golden.npz")
     np.savez_compressed(path, names=np.array([n for n, _, _ in cases()]), **arrays)
     print(f"wrote {path} ({path.stat().st_size} bytes)")
 

@@ -7,8 +7,8 @@ model shape):
   * config 1: the full 32-step CFG generation with the reference's noise
     stream, against the oracle's generation stored in
     tests/golden/generation_golden.npz (made by make_generation_golden.py);
-    and step by step on the oracle's own trajectory (the same ids into both
-    forwards at every step);
+  * configs 1 and 2: step by step on the oracle's own 32-step trajectory
+    (the same ids into both forwards at every step);
   * configs 2, 3 and 5: one CFG forward each against the oracle's forward
     (computed here), logits within 2e-2 absolute; the scores of those
     logits with exact argmax outside the float32 tie band;
@@ -28,10 +28,10 @@ trajectories part, not how close the arithmetic is, so it is reported
 (next to the reversed-sum restatement's figure) and asserted only on
 what does not depend on the trajectory: valid codes and every step
 unmasking exactly its scheduled count.  The parity bar is asserted step
-by step on the oracle's own config-1 trajectory (the same ids into both
-forwards at every step): predictions at the masked positions at least as
-close as the reversed-sum restatement's, or 99 %, and 99 % of the chosen
-positions.  Every comparison prints its figure.
+by step on the oracle's own config-1 and config-2 trajectories (the same ids
+into both forwards at every step): predictions at the masked positions at
+least as close as the reversed-sum restatement's, or 99 %, and 99 % of the
+chosen positions.  Every comparison prints its figure.
 """
 from __future__ import annotations
 
@@ -100,16 +100,17 @@ def test_generate_config1_full_model_matches_oracle(full, golden, golden_data):
     print(f"config 1: the reversed-sum oracle agrees {v_codes:.4f} / {v_when:.4f}")
 
 
-def test_config1_steps_on_the_oracle_trajectory(full, golden, golden_data):
-    """Every step of the oracle's config-1 generation, fed to the GPU with
-    the oracle's ids: the predictions at the masked positions, and the
-    positions the selection picks from the GPU's confidences with the
+@pytest.mark.parametrize("case", ["c1", "c2"])
+def test_steps_on_the_oracle_trajectory(full, golden, golden_data, case):
+    """Every step of the oracle's config-1 / config-2 generation, fed to the
+    GPU with the oracle's ids: the predictions at the masked positions, and
+    the positions the selection picks from the GPU's confidences with the
     step's reference noise, against the oracle's."""
     from oracle import binding
-    inp, seed, _, _ = golden["c1"]
-    step_ids = golden_data["c1_step_ids"]
-    step_pred = golden_data["c1_step_prediction"]
-    step_conf = golden_data["c1_step_confidence"]
+    inp, seed, _, _ = golden[case]
+    step_ids = golden_data[f"{case}_step_ids"]
+    step_pred = golden_data[f"{case}_step_prediction"]
+    step_conf = golden_data[f"{case}_step_confidence"]
     F = inp.target_frames
     total = 8 * F
     sched = binding.schedule(total, 32, 0.1)
@@ -134,8 +135,8 @@ def test_config1_steps_on_the_oracle_trajectory(full, golden, golden_data):
         picked_total += len(want)
     pred_agree = same_pred / masked_total
     pick_agree = same_pick / picked_total
-    variant = float(golden_data["c1_variant_agreement"][2])
-    print(f"config 1 step by step: predictions {pred_agree:.4f} equal at masked positions "
+    variant = float(golden_data[f"{case}_variant_agreement"][2])
+    print(f"{case} step by step: predictions {pred_agree:.4f} equal at masked positions "
           f"({masked_total - same_pred} of {masked_total} differ), chosen positions "
           f"{pick_agree:.4f}; the reversed-sum oracle's predictions {variant:.4f}")
     assert pred_agree >= min(0.99, variant)
