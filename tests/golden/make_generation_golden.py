@@ -9,6 +9,8 @@ seed as in decoding.cpp:64-68,84-85):
             100 masked frames, generation seed 0;
   c2        BASELINE config 2: 120 text ids U[0, 151935] (numpy seed 1),
             250 masked frames, generation seed 1;
+  c3        BASELINE config 3: 180 text ids and 150 frames of reference codes
+            U[0, 1023] (numpy seed 2), 375 masked frames, generation seed 2;
   c4_<i>    six utterances of the BASELINE config-4 set (64 utterances,
             numpy seed 4: F ~ U[50, 750], text = round(0.4 F), half with
             125-250 reference frames), the six with the fewest packed rows
@@ -17,7 +19,7 @@ Per case it stores the conditional ids, audio_start, the frame count, the
 seed and the oracle's codes and unmasked_at ([8][F] int32 each).  The GPU
 test (tests/test_gpu_fullshape.py) generates the same inputs and compares.
 
-For configs 1 and 2 it also stores the oracle's trajectory: per step the
+For configs 1, 2 and 3 it also stores the oracle's trajectory: per step the
 ids the forward pass saw and the scoring's predictions and confidences, so
 the GPU can be compared step by step on identical inputs.
 
@@ -57,6 +59,10 @@ def cases():
     rng = np.random.default_rng(1)
     inp = ConditionalInput.build(rng.integers(0, VOCAB, size=120).tolist(), None, 250)
     out.append(("c2", inp, 1))
+    rng = np.random.default_rng(2)
+    text = rng.integers(0, VOCAB, size=180).tolist()
+    ref = rng.integers(0, 1024, size=(8, 150)).astype(np.int32)
+    out.append(("c3", ConditionalInput.build(text, ref, 375), 2))
     # The config-4 set, drawn exactly as bench.py's batched_set().
     rng = np.random.default_rng(4)
     frames = rng.integers(50, 751, size=64)
@@ -106,7 +112,7 @@ def main() -> None:
         lib.oc_set_accumulation_order(1)
         v_codes, v_when = model.generate(inp.ids, inp.audio_start, inp.target_frames, seed=seed)
         agreement = [float((v_codes == codes).mean()), float((v_when == when).mean())]
-        if name in ("c1", "c2"):
+        if name in ("c1", "c2", "c3"):
             arrays[f"{name}_step_ids"] = step_ids
             arrays[f"{name}_step_prediction"] = step_pred
             arrays[f"{name}_step_confidence"] = step_conf

@@ -7,8 +7,8 @@ model shape):
   * config 1: the full 32-step CFG generation with the reference's noise
     stream, against the oracle's generation stored in
     tests/golden/generation_golden.npz (made by make_generation_golden.py);
-  * configs 1 and 2: step by step on the oracle's own 32-step trajectory
-    (the same ids into both forwards at every step);
+  * configs 1, 2 and 3 (with reference codes): step by step on the oracle's
+    own 32-step trajectory (the same ids into both forwards at every step);
   * configs 2, 3 and 5: one CFG forward each against the oracle's forward
     (computed here), logits within 2e-2 absolute; the scores of those
     logits with exact argmax outside the float32 tie band;
@@ -28,7 +28,7 @@ trajectories part, not how close the arithmetic is, so it is reported
 (next to the reversed-sum restatement's figure) and asserted only on
 what does not depend on the trajectory: valid codes and every step
 unmasking exactly its scheduled count.  The parity bar is asserted step
-by step on the oracle's own config-1 and config-2 trajectories (the same ids
+by step on the oracle's own config-1, 2 and 3 trajectories (the same ids
 into both forwards at every step): predictions at the masked positions at
 least as close as the reversed-sum restatement's, or 99 %, and 99 % of the
 chosen positions.  Every comparison prints its figure.
@@ -100,9 +100,9 @@ def test_generate_config1_full_model_matches_oracle(full, golden, golden_data):
     print(f"config 1: the reversed-sum oracle agrees {v_codes:.4f} / {v_when:.4f}")
 
 
-@pytest.mark.parametrize("case", ["c1", "c2"])
+@pytest.mark.parametrize("case", ["c1", "c2", "c3"])
 def test_steps_on_the_oracle_trajectory(full, golden, golden_data, case):
-    """Every step of the oracle's config-1 / config-2 generation, fed to the
+    """Every step of the oracle's config-1 / 2 / 3 generation, fed to the
     GPU with the oracle's ids: the predictions at the masked positions, and
     the positions the selection picks from the GPU's confidences with the
     step's reference noise, against the oracle's."""
