@@ -415,14 +415,16 @@ def _work_list(lengths, per_item):
     return torch.tensor(items, dtype=torch.int32)
 
 
-@pytest.mark.parametrize("form", ["pair", "single"])
+@pytest.mark.parametrize("form", ["pair", "pair_t", "single"])
 @pytest.mark.parametrize("seed,count,lo,hi", [(0, 40, 50, 900), (1, 300, 1, 300),
                                               (2, 12, 1, 140)])
-def test_attention_work_list(seed, count, lo, hi, form):
+def test_attention_work_list(monkeypatch, seed, count, lo, hi, form):
     """The generator's form of the attention: a work list of query-tile
     pairs (items of one or two tiles, one or many key tiles, the last key
     tile cut at any length) or of single tiles, one CTA per (item, head).
-    Against float64."""
+    The transposed pair form (pair_t) runs the same list.  Against float64."""
+    if form == "pair_t":
+        monkeypatch.setenv("OV_ATTN_PAIR", "t")
     rng = np.random.default_rng(seed)
     lengths = [int(v) for v in rng.integers(lo, hi + 1, size=count)]
     heads, kv = 16, 8
